@@ -1,0 +1,99 @@
+/*
+ * tilegen_b200 C ABI: the int8_convrot hot path as prebuilt sm_100a kernels.
+ *
+ * Plain pointers and sizes only.  Every compute entry point
+ *   - takes device pointers and a cudaStream_t passed as `void *stream`
+ *     (NULL = the legacy default stream) and only enqueues work on it: no host
+ *     synchronisation, no allocation (callers own every buffer, so the calls
+ *     can be captured in CUDA graphs);
+ *   - returns a tg_status; nothing is launched when it is not TG_OK.
+ * Device-side failures (a bounded wait that gave up) are recorded in a device
+ * status word that tg_device_status() reads.
+ *
+ * The Python package binds these with ctypes (tilegen_b200/_lib.py); the
+ * reference-side binding a maintainer would add is shown in INTEGRATION.md.
+ */
+#ifndef TILEGEN_B200_H
+#define TILEGEN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  TG_OK = 0,
+  TG_ERR_INVALID_ARG = 1,   /* null pointer, negative size, bad dtype code */
+  TG_ERR_UNSUPPORTED = 2,   /* shape/group outside what the kernel handles */
+  TG_ERR_MISALIGNED = 3,    /* a pointer is not 16-byte aligned */
+  TG_ERR_CUDA = 4,          /* a CUDA runtime/driver call failed (launch etc.) */
+  TG_ERR_DEVICE_TIMEOUT = 5 /* tg_device_status(): a kernel's bounded wait expired */
+} tg_status;
+
+typedef enum { TG_DT_F32 = 0, TG_DT_F16 = 1, TG_DT_BF16 = 2 } tg_dtype;
+
+/* Library version, (major << 16) | minor. */
+int tg_version(void);
+
+/* Human-readable name of a tg_status value. */
+const char *tg_status_string(int status);
+
+/*
+ * Fused group-Hadamard rotation + row-wise symmetric int8 quantisation.
+ *
+ * Replaces the reference's NVRTC kernel launch `quantize_convrot_native`
+ * (tilegen/kernels/int8_convrot.py:196-230; kernel `fht_quant` at :47-104), and
+ * also serves the weight side `quantize_convrot_weight`
+ * (tilegen/quant/weight.py:14-39), which is the same operation on W rows.
+ *
+ *   x      [M, K] row-major, dtype x_dtype (TG_DT_F16 or TG_DT_BF16), 16-B aligned
+ *   group  4, 16, 64 or 256 (a power of four, as tilegen/kernels/hadamard.py:18-22);
+ *          K must be a multiple of 256 and at most tg_rotate_quant_max_k()
+ *   q      [M, K] int8 out: clamp(rint(rot * 1/(sqrt(G)*scale)), -128, 127)
+ *   scale  [M] fp32 out:   max(absmax(rot_unnormalised) / (127*sqrt(G)), 1e-30)
+ * The rotation is evaluated in fp32 in the reference kernel's butterfly order,
+ * so the result is bit-identical to it for fp16 input; bf16 is read directly
+ * (the reference first casts bf16 to fp16, int8_convrot.py:204-206).
+ * M == 0 is a no-op.
+ */
+int tg_rotate_quant(const void *x, int x_dtype, int64_t M, int64_t K, int group, int8_t *q, float *scale,
+                    void *stream);
+
+/* Largest K tg_rotate_quant accepts (a multiple of 256). */
+int64_t tg_rotate_quant_max_k(void);
+
+/*
+ * INT8 GEMM with the dequantisation fused into the epilogue (tcgen05 kind::i8,
+ * int32 accumulators in tensor memory).
+ *
+ * Replaces `int8_matmul_dequant_chunked` (tilegen/quant/int8_ops.py:22-70):
+ *   acc[m,n] = sum_k xq[m,k] * wq[n,k]                    (exact int32)
+ *   out[m,n] = ((float(acc) * xscale[m]) * wscale[n]) + bias[n]
+ * in fp32 with one rounding per operation (no FMA), stored as out_dtype with
+ * round-to-nearest-even: bit-identical to the reference's torch sequence.
+ *
+ *   xq [M, K] int8, wq [N, K] int8 (both K-major, 16-B aligned; K % 16 == 0)
+ *   xscale [M] fp32; wscale fp32 of wscale_numel = 1 (broadcast) or N
+ *   bias [N] of bias_dtype (TG_DT_F32/F16/BF16) or NULL
+ *   out [M, N] of out_dtype (TG_DT_F32/F16/BF16); N*sizeof(out) % 16 == 0
+ * M == 0 is a no-op.  No temporary memory is used, so the reference's chunking
+ * argument has nothing to bound.
+ */
+int tg_int8_gemm_dequant(const int8_t *xq, const float *xscale, const int8_t *wq, const float *wscale,
+                         int64_t wscale_numel, const void *bias, int bias_dtype, int64_t M, int64_t N,
+                         int64_t K, int out_dtype, void *out, void *stream);
+
+/*
+ * Read (and optionally clear) the device status word of `device`, which
+ * kernels set when a bounded wait expires.  Synchronises the device.
+ * *bits receives the raw word (0 = healthy); returns TG_ERR_DEVICE_TIMEOUT when
+ * it is non-zero, TG_OK otherwise.
+ */
+int tg_device_status(int device, uint32_t *bits, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TILEGEN_B200_H */

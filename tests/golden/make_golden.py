@@ -1,0 +1,138 @@
+"""Generate the golden fixtures in this folder from the reference implementation.
+
+Run from the repository root in a container that has the reference sources:
+
+    python tests/golden/make_golden.py /root/reference
+
+It imports the reference's own pure-torch functions (they run on the CPU) and
+records their outputs on small seeded inputs:
+
+* ``quant.npz``   - ``tilegen.kernels.int8_convrot._eager_quantize(x.float(), G)``
+  (int8_convrot.py:289-302) for fp32/fp16/bf16 inputs, several K and G, plus rows
+  with zeros, tiny and huge values.
+* ``weight.npz``  - ``tilegen.quant.weight.quantize_convrot_weight(W, 256)``
+  (weight.py:14-39) on fp32 weights.
+* ``gemm.npz``    - ``tilegen.quant.int8_ops.int8_matmul_dequant_chunked``
+  (int8_ops.py:22-70) through CPU ``torch._int_mm``: fp16/bf16/fp32 outputs,
+  with and without bias, per-channel and scalar weight scales, small chunk caps.
+* ``config1.npz`` - the CPU reference workload end to end: x fp32 [256, 5120]
+  N(0,1) with 1 % outlier channels x30, W fp32 [5120, 5120] N(0, 0.02), seed 0;
+  Y = dequant(int8 GEMM).  Stored: input checksums, both scale vectors, the
+  first rows of the codes and of Y, and Y's Frobenius norm.
+
+The fixtures are committed; the tests never read the reference at run time.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+
+
+def _sha(t: torch.Tensor) -> str:
+    return hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+
+
+def _u16(t: torch.Tensor) -> np.ndarray:
+    """fp16/bf16 tensor -> its raw 16-bit patterns (numpy has no bf16)."""
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    sys.path.append(REPO)
+    from tilegen.kernels.int8_convrot import _eager_quantize  # reference
+    from tilegen.quant.int8_ops import int8_matmul_dequant_chunked  # reference
+    from tilegen.quant.weight import quantize_convrot_weight  # reference
+    assert os.path.realpath(sys.modules["tilegen"].__file__).startswith(os.path.realpath(ref_root))
+    from tilegen_b200.synthetic import gaussian_weight, outlier_activations
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    dts = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+
+    # ---- activation quantizer -------------------------------------------------
+    quant = {}
+    cases = [
+        # name, M, K, G, dtype, seed
+        ("a", 8, 5120, 256, "f16", 1),
+        ("b", 6, 13824, 256, "bf16", 2),
+        ("c", 16, 1536, 256, "f32", 3),
+        ("d", 8, 3072, 64, "f16", 4),
+        ("e", 8, 1024, 16, "bf16", 5),
+        ("f", 4, 512, 4, "f32", 6),
+        ("g", 5, 256, 256, "f16", 7),
+    ]
+    for name, m, k, g, dt, seed in cases:
+        x = outlier_activations(m, k, seed=seed, dtype=dts[dt])
+        if name == "g":
+            x[0].zero_()                          # all-zero row -> scale clamps to 1e-30
+            x[1] = x[1].float().mul(1e-6).to(x.dtype)  # tiny values
+            x[2] = x[2].float().mul(2000.0).clamp(-60000, 60000).to(x.dtype)  # near fp16 max
+        q, s = _eager_quantize(x.float(), g)
+        quant[f"{name}_meta"] = np.array([m, k, g, list(dts).index(dt)], dtype=np.int64)
+        quant[f"{name}_x"] = x.numpy() if dt == "f32" else _u16(x)
+        quant[f"{name}_q"] = q.numpy()
+        quant[f"{name}_scale"] = s.numpy()
+    np.savez_compressed(os.path.join(HERE, "quant.npz"), **quant)
+
+    # ---- weight quantizer -----------------------------------------------------
+    w = gaussian_weight(16, 5120, seed=11)
+    wq, ws = quantize_convrot_weight(w.float(), 256)
+    np.savez_compressed(os.path.join(HERE, "weight.npz"), w=w.numpy(), wq=wq.numpy(), wscale=ws.numpy())
+
+    # ---- int8 GEMM + dequant ----------------------------------------------------
+    gemm = {}
+    gcases = [
+        # name, M, N, K, out, bias, scalar wscale, chunk bytes
+        ("a", 33, 72, 512, "f16", True, False, 256 << 20),
+        ("b", 17, 64, 5120, "bf16", False, False, 256 << 20),
+        ("c", 40, 48, 256, "f32", True, True, 256 << 20),
+        ("d", 130, 136, 1024, "f16", False, False, 4096),  # forces many row chunks
+    ]
+    for name, m, n, k, out, has_bias, scalar, cap in gcases:
+        g = torch.Generator().manual_seed(100 + m)
+        xq = torch.randint(-128, 128, (m, k), generator=g, dtype=torch.int8)
+        wq_ = torch.randint(-128, 128, (n, k), generator=g, dtype=torch.int8)
+        xs = torch.rand(m, generator=g) * 0.02 + 1e-4
+        wsc = torch.rand(1 if scalar else n, generator=g) * 0.01 + 1e-5
+        bias = (torch.randn(n, generator=g) if has_bias else None)
+        y = int8_matmul_dequant_chunked(xq, xs, wq_, wsc if not scalar else wsc.reshape(()),
+                                        bias, dts[out], max_temp_bytes=cap)
+        gemm[f"{name}_meta"] = np.array([m, n, k, list(dts).index(out), int(has_bias), int(scalar)], dtype=np.int64)
+        gemm[f"{name}_xq"] = xq.numpy()
+        gemm[f"{name}_wq"] = wq_.numpy()
+        gemm[f"{name}_xscale"] = xs.numpy()
+        gemm[f"{name}_wscale"] = wsc.numpy()
+        gemm[f"{name}_bias"] = bias.numpy() if has_bias else np.zeros(0, np.float32)
+        gemm[f"{name}_y"] = y.numpy() if out == "f32" else _u16(y)
+    np.savez_compressed(os.path.join(HERE, "gemm.npz"), **gemm)
+
+    # ---- config 1: the CPU reference workload end to end ------------------------
+    x = outlier_activations(256, 5120, seed=0, dtype=torch.float32)
+    w = gaussian_weight(5120, 5120, seed=0)
+    xq, xs = _eager_quantize(x, 256)
+    wq, ws = quantize_convrot_weight(w, 256)
+    y = int8_matmul_dequant_chunked(xq, xs, wq, ws, None, torch.float32)
+    dense = x @ w.t()
+    rel = ((y - dense).norm() / dense.norm()).item()
+    np.savez_compressed(
+        os.path.join(HERE, "config1.npz"),
+        x_sha=np.array(_sha(x)), w_sha=np.array(_sha(w)),
+        xscale=xs.numpy(), wscale=ws.numpy(),
+        xq_head=xq[:8].numpy(), wq_head=wq[:8].numpy(),
+        y_head=y[:8].numpy(), y_norm=np.array(y.norm().item()),
+        rel_vs_dense=np.array(rel),
+    )
+    print("config1 rel-Frobenius vs fp32 dense:", rel)
+    for f in ("quant.npz", "weight.npz", "gemm.npz", "config1.npz"):
+        print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

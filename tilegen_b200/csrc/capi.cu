@@ -1,0 +1,305 @@
+// Host side of the tilegen_b200 C ABI (include/tilegen_b200.h): argument
+// checks, launch-shape selection, TMA descriptor encoding and the launches.
+// One translation unit holds every kernel so they share the device status word.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm_i8.cuh"
+#include "rotquant.cuh"
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int64_t kRotQuantMaxK = 32768;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+};
+
+bool current_device(int* dev, DeviceInfo* info) {
+  static DeviceInfo cache[kMaxDevices];
+  if (cudaGetDevice(dev) != cudaSuccess || *dev < 0 || *dev >= kMaxDevices) return false;
+  if (cache[*dev].sms == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, *dev) != cudaSuccess) return false;
+    cache[*dev].sms = v;
+  }
+  *info = cache[*dev];
+  return true;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 2-D tiled tensor map, innermost dimension first.
+bool make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Per-(kernel, device) one-time attribute setup.
+template <typename K>
+bool ensure_smem_attr(K kernel, int dev, uint32_t bytes, uint32_t* done_bytes) {
+  if (done_bytes[dev] >= bytes) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)) != cudaSuccess)
+    return false;
+  done_bytes[dev] = bytes;
+  return true;
+}
+
+// ------------------------------------------------------------------ rotate+quant
+template <int NST, bool BF16>
+int launch_rotquant_t(const CUtensorMap& tm, const tg::RotQuantParams& p, int threads, uint32_t smem, int dev,
+                      int sms, cudaStream_t st) {
+  static uint32_t attr_done[kMaxDevices];
+  static int occ_cache[kMaxDevices][4][2];  // [dev][stages-1..][threads>256]
+  auto kern = tg::rotquant_kernel<NST, BF16>;
+  if (!ensure_smem_attr(kern, dev, smem, attr_done)) return TG_ERR_CUDA;
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem) != cudaSuccess || occ < 1)
+    return TG_ERR_CUDA;
+  (void)occ_cache;
+  const int64_t grid64 = std::min<int64_t>(p.nbatches, int64_t(sms) * occ);
+  kern<<<dim3(unsigned(grid64)), dim3(threads), smem, st>>>(tm, p);
+  return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
+}
+
+int gcd_int(int a, int b) {
+  while (b) {
+    const int t = a % b;
+    a = b;
+    b = t;
+  }
+  return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tg_version(void) { return (0 << 16) | 1; }
+
+const char* tg_status_string(int s) {
+  switch (s) {
+    case TG_OK: return "ok";
+    case TG_ERR_INVALID_ARG: return "invalid argument";
+    case TG_ERR_UNSUPPORTED: return "unsupported shape or group size";
+    case TG_ERR_MISALIGNED: return "pointer not 16-byte aligned";
+    case TG_ERR_CUDA: return "CUDA call failed";
+    case TG_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait expired";
+    default: return "unknown status";
+  }
+}
+
+int64_t tg_rotate_quant_max_k(void) { return kRotQuantMaxK; }
+
+int tg_rotate_quant(const void* x, int x_dtype, int64_t M, int64_t K, int group, int8_t* q, float* scale,
+                    void* stream) {
+  if (M < 0 || K <= 0) return TG_ERR_INVALID_ARG;
+  if (x_dtype != TG_DT_F16 && x_dtype != TG_DT_BF16) return TG_ERR_INVALID_ARG;
+  int nst;
+  switch (group) {
+    case 4: nst = 1; break;
+    case 16: nst = 2; break;
+    case 64: nst = 3; break;
+    case 256: nst = 4; break;
+    default: return TG_ERR_UNSUPPORTED;
+  }
+  if (K % 256 != 0 || K > kRotQuantMaxK) return TG_ERR_UNSUPPORTED;
+  if (M == 0) return TG_OK;
+  if (!x || !q || !scale) return TG_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(q) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return TG_ERR_MISALIGNED;
+  const int cpr = int(K / 64);
+  if (M * int64_t(cpr) >= (int64_t(1) << 31)) return TG_ERR_UNSUPPORTED;
+
+  // Rows per batch: the fewest that fill whole warps to within 5 %.
+  int R = 1;
+  for (int r = 1; r <= 8; ++r) {
+    const int act = r * cpr;
+    const int thr = (act + 31) / 32 * 32;
+    if (thr > 512) break;
+    if ((thr - act) * 20 <= act) {
+      R = r;
+      break;
+    }
+  }
+  const int active = R * cpr;
+  const int threads = (active + 31) / 32 * 32;
+  if (threads > 512) return TG_ERR_UNSUPPORTED;
+  int box = active;
+  if (box > 256) {
+    box = 4;
+    for (int d = 256; d >= 4; --d)
+      if (active % d == 0) {
+        box = d;
+        break;
+      }
+  }
+  const uint32_t stage_bytes = uint32_t(threads) * 128u;
+  int stages = int((110u * 1024u) / stage_bytes);
+  stages = stages < 2 ? 2 : (stages > 4 ? 4 : stages);
+  const uint32_t smem = 1024u + uint32_t(stages) * stage_bytes + uint32_t(stages) * 8u + uint32_t(3 * R) * 4u;
+
+  int dev;
+  DeviceInfo info;
+  if (!current_device(&dev, &info)) return TG_ERR_CUDA;
+
+  CUtensorMap tm;
+  if (!make_tmap_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, x, 64, uint64_t(M) * uint64_t(cpr), 128, 64,
+                    uint32_t(box), CU_TENSOR_MAP_SWIZZLE_128B))
+    return TG_ERR_CUDA;
+
+  tg::RotQuantParams p;
+  p.q = q;
+  p.scale = scale;
+  p.M = M;
+  p.K = int(K);
+  p.cpr = cpr;
+  p.rows_per_batch = R;
+  p.active = active;
+  p.box_lines = box;
+  p.boxes = active / box;
+  p.nbatches = (M + R - 1) / R;
+  p.stages = stages;
+  p.stage_bytes = stage_bytes;
+  p.seg = gcd_int(cpr, 32);
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf = x_dtype == TG_DT_BF16;
+  switch (nst) {
+    case 1: return bf ? launch_rotquant_t<1, true>(tm, p, threads, smem, dev, info.sms, st)
+                      : launch_rotquant_t<1, false>(tm, p, threads, smem, dev, info.sms, st);
+    case 2: return bf ? launch_rotquant_t<2, true>(tm, p, threads, smem, dev, info.sms, st)
+                      : launch_rotquant_t<2, false>(tm, p, threads, smem, dev, info.sms, st);
+    case 3: return bf ? launch_rotquant_t<3, true>(tm, p, threads, smem, dev, info.sms, st)
+                      : launch_rotquant_t<3, false>(tm, p, threads, smem, dev, info.sms, st);
+    default: return bf ? launch_rotquant_t<4, true>(tm, p, threads, smem, dev, info.sms, st)
+                       : launch_rotquant_t<4, false>(tm, p, threads, smem, dev, info.sms, st);
+  }
+}
+
+}  // extern "C"
+
+namespace {
+
+template <int OUT, bool HAS_BIAS>
+int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const tg::GemmParams& p,
+                  int dev, int sms, cudaStream_t st) {
+  static uint32_t attr_done[kMaxDevices];
+  auto kern = tg::gemm_i8_dequant_kernel<OUT, HAS_BIAS>;
+  if (!ensure_smem_attr(kern, dev, tg::gemm::SMEM_BYTES, attr_done)) return TG_ERR_CUDA;
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = tiles < sms ? tiles : sms;
+  kern<<<dim3(unsigned(grid)), dim3(tg::gemm::THREADS), tg::gemm::SMEM_BYTES, st>>>(ta, tb, to, p);
+  return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tg_int8_gemm_dequant(const int8_t* xq, const float* xscale, const int8_t* wq, const float* wscale,
+                         int64_t wscale_numel, const void* bias, int bias_dtype, int64_t M, int64_t N, int64_t K,
+                         int out_dtype, void* out, void* stream) {
+  using namespace tg::gemm;
+  if (M < 0 || N <= 0 || K <= 0) return TG_ERR_INVALID_ARG;
+  if (out_dtype != TG_DT_F32 && out_dtype != TG_DT_F16 && out_dtype != TG_DT_BF16) return TG_ERR_INVALID_ARG;
+  if (bias && bias_dtype != TG_DT_F32 && bias_dtype != TG_DT_F16 && bias_dtype != TG_DT_BF16)
+    return TG_ERR_INVALID_ARG;
+  if (wscale_numel != 1 && wscale_numel != N) return TG_ERR_INVALID_ARG;
+  const int esz = out_dtype == TG_DT_F32 ? 4 : 2;
+  if (K % 16 != 0 || (N * esz) % 16 != 0) return TG_ERR_UNSUPPORTED;
+  if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) || K >= (int64_t(1) << 31)) return TG_ERR_UNSUPPORTED;
+  if (M == 0) return TG_OK;
+  if (!xq || !xscale || !wq || !wscale || !out) return TG_ERR_INVALID_ARG;
+  if (!aligned16(xq) || !aligned16(wq) || !aligned16(out)) return TG_ERR_MISALIGNED;
+  if ((reinterpret_cast<uintptr_t>(xscale) & 3u) || (reinterpret_cast<uintptr_t>(wscale) & 3u))
+    return TG_ERR_MISALIGNED;
+
+  int dev;
+  DeviceInfo info;
+  if (!current_device(&dev, &info)) return TG_ERR_CUDA;
+
+  CUtensorMap ta, tb, to;
+  if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, uint64_t(K), uint64_t(M), uint64_t(K), BK, BM,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return TG_ERR_CUDA;
+  if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, uint64_t(K), uint64_t(N), uint64_t(K), BK, BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return TG_ERR_CUDA;
+  const CUtensorMapDataType odt = out_dtype == TG_DT_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                  : out_dtype == TG_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (!make_tmap_2d(&to, odt, out, uint64_t(N), uint64_t(M), uint64_t(N) * esz, uint32_t(128 / esz), 32,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return TG_ERR_CUDA;
+
+  tg::GemmParams p;
+  p.xscale = xscale;
+  p.wscale = wscale;
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.wscale_bcast = wscale_numel == 1 ? 1 : 0;
+  p.M = int(M);
+  p.N = int(N);
+  p.K = int(K);
+  p.m_tiles = int((M + BM - 1) / BM);
+  p.n_tiles = int((N + BN - 1) / BN);
+  p.k_blocks = int((K + BK - 1) / BK);
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool hb = bias != nullptr;
+  switch (out_dtype) {
+    case TG_DT_F32: return hb ? launch_gemm_t<0, true>(ta, tb, to, p, dev, info.sms, st)
+                              : launch_gemm_t<0, false>(ta, tb, to, p, dev, info.sms, st);
+    case TG_DT_F16: return hb ? launch_gemm_t<1, true>(ta, tb, to, p, dev, info.sms, st)
+                              : launch_gemm_t<1, false>(ta, tb, to, p, dev, info.sms, st);
+    default: return hb ? launch_gemm_t<2, true>(ta, tb, to, p, dev, info.sms, st)
+                       : launch_gemm_t<2, false>(ta, tb, to, p, dev, info.sms, st);
+  }
+}
+
+int tg_device_status(int device, uint32_t* bits, int clear) {
+  if (!bits) return TG_ERR_INVALID_ARG;
+  int prev;
+  if (cudaGetDevice(&prev) != cudaSuccess) return TG_ERR_CUDA;
+  if (device != prev && cudaSetDevice(device) != cudaSuccess) return TG_ERR_CUDA;
+  unsigned int v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, tg::g_device_status, sizeof(v));
+  if (e == cudaSuccess && clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(tg::g_device_status, &zero, sizeof(zero));
+  }
+  if (device != prev) cudaSetDevice(prev);
+  if (e != cudaSuccess) return TG_ERR_CUDA;
+  *bits = v;
+  return v ? TG_ERR_DEVICE_TIMEOUT : TG_OK;
+}
+
+}  // extern "C"

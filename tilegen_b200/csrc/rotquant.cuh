@@ -1,0 +1,300 @@
+// Fused group-Hadamard rotation + row-wise int8 quantisation (sm_100a).
+//
+// Algorithm (the reference kernel `fht_quant`, tilegen/kernels/int8_convrot.py:47-104):
+// per group of G = 4^NST elements, NST radix-4 butterfly stages on the H4 of
+// tilegen/kernels/hadamard.py:15, stage s at stride 4^s, every output summed left
+// to right as at int8_convrot.py:74-77; then the row absmax, the scale
+// absmax/(127*sqrt(G)) clamped at 1e-30, and codes rint(v / (sqrt(G)*scale)).
+// The same fp32 operations in the same order make the codes and scales
+// bit-identical to that kernel (and to the C oracle that restates it).
+//
+// B200 layout:
+//  * A persistent CTA owns R rows at a time ("a batch").  One thread owns one
+//    64-element chunk of a row (its 128-byte "line"), so a row is K/64 threads
+//    and a batch is R*K/64 threads; R is picked so the batch fills whole warps.
+//  * Batches stream HBM -> shared memory with 2-D TMA copies (128-byte swizzle)
+//    into a ring of `stages` buffers completed on mbarriers, so several batches
+//    are in flight per SM while the current one is rotated.
+//  * Stages 0..2 (index bits 0..5) run in registers on the thread's own 64
+//    values.  For G=256 stage 3 needs the four chunks of a group: the four
+//    threads swap 16-value blocks through the warp's own (already consumed)
+//    slice of the stage buffer, so that afterwards each holds one 16-wide
+//    column block for all four inputs of the last butterfly, in input order.
+//  * Row absmax: warp shuffles over the row's lanes, then one shared-memory
+//    atomicMax per segment and a CTA barrier.  The rotated values never leave
+//    registers; the codes are packed 16 per 128-bit store straight to HBM.
+#pragma once
+
+#include "common.cuh"
+
+namespace tg {
+
+struct RotQuantParams {
+  int8_t* q;
+  float* scale;
+  int64_t M;
+  int K;
+  int cpr;               // 64-element chunks per row = K / 64
+  int rows_per_batch;    // R
+  int active;            // threads that own a chunk = R * cpr
+  int box_lines;         // 128-byte lines per TMA box
+  int boxes;             // TMA boxes per batch
+  int64_t nbatches;      // ceil(M / R)
+  int stages;            // shared-memory ring depth
+  uint32_t stage_bytes;  // bytes per ring slot = blockDim.x * 128 (a multiple of 1024)
+  int seg;               // lanes per absmax shuffle segment = gcd(cpr, 32)
+};
+
+// One radix-4 butterfly, each output evaluated exactly as
+//   y0 = a0 + a1 + a2 - a3, y1 = a0 + a1 - a2 + a3,
+//   y2 = a0 - a1 + a2 + a3, y3 = -a0 + a1 + a2 + a3   (left to right),
+// with the shared partial sums factored out: (-a0 + a1) == -(a0 - a1) and
+// (-d) + a2 == a2 - d hold exactly in IEEE arithmetic.
+__device__ __forceinline__ void bfly4(float& a0, float& a1, float& a2, float& a3) {
+  const float s = __fadd_rn(a0, a1);
+  const float d = __fsub_rn(a0, a1);
+  const float y0 = __fsub_rn(__fadd_rn(s, a2), a3);
+  const float y1 = __fadd_rn(__fsub_rn(s, a2), a3);
+  const float y2 = __fadd_rn(__fadd_rn(d, a2), a3);
+  const float y3 = __fadd_rn(__fsub_rn(a2, d), a3);
+  a0 = y0;
+  a1 = y1;
+  a2 = y2;
+  a3 = y3;
+}
+
+// Radix-4 stage ST (stride 4^ST) over 64 values held in registers.
+template <int ST>
+__device__ __forceinline__ void stage64(float (&v)[64]) {
+  constexpr int stride = 1 << (2 * ST);
+#pragma unroll
+  for (int b = 0; b < 16; ++b) {
+    const int low = b % stride;
+    const int high = b / stride;
+    const int base = high * 4 * stride + low;
+    bfly4(v[base], v[base + stride], v[base + 2 * stride], v[base + 3 * stride]);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ void unpack8(const uint4 w, float* f) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (BF16) {
+      f[2 * i] = __uint_as_float(u[i] << 16);
+      f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+    } else {
+      __half2 h = *reinterpret_cast<const __half2*>(&u[i]);
+      const float2 t = __half22float2(h);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+}
+
+// Code for one value, returned in the low byte: clamp(rint(x*inv), -128, 127).
+// Adding 1.5*2^23 rounds to the nearest integer (ties to even) and leaves it in
+// the low mantissa bits; the lower clamp also maps NaN to -128 as fmaxf does in
+// the reference.  No upper clamp is needed: |x| <= absmax and
+// inv = 1/(sqrt(G)*scale) with scale >= absmax/(127*sqrt(G)) bound x*inv by
+// 127*(1+2^-22), which rounds to 127.
+__device__ __forceinline__ uint32_t code_bits(float x, float inv) {
+  float t = __fmul_rn(x, inv);
+  t = fmaxf(t, -128.0f);
+  return __float_as_uint(__fadd_rn(t, 12582912.0f));
+}
+
+__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+template <int NST, bool BF16>
+__global__ void __launch_bounds__(512) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
+                                                       const RotQuantParams p) {
+  constexpr float kRoot = float(1 << NST);          // sqrt(G)
+  constexpr float kQmaxRoot = 127.0f * float(1 << NST);  // 2032 for G = 256
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(p.stages) * p.stage_bytes);
+  unsigned* rowmax = reinterpret_cast<unsigned*>(full + p.stages);  // [3][R]
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int R = p.rows_per_batch;
+
+  if (tid == 0) {
+    prefetch_tmap(&tmx);
+    for (int s = 0; s < p.stages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  for (int i = tid; i < 3 * R; i += blockDim.x) rowmax[i] = 0u;
+  __syncthreads();
+
+  const int64_t first = blockIdx.x;
+  const int64_t step = gridDim.x;
+  const uint32_t batch_bytes = uint32_t(p.boxes) * uint32_t(p.box_lines) * 128u;
+
+  auto issue = [&](int64_t batch, int s) {
+    mbar_arrive_expect_tx(&full[s], batch_bytes);
+    uint8_t* dst = smem + size_t(s) * p.stage_bytes;
+    const int64_t line0 = batch * int64_t(p.active);
+    for (int b = 0; b < p.boxes; ++b)
+      tma_load_2d(dst + size_t(b) * p.box_lines * 128, &tmx, &full[s], 0, int(line0 + int64_t(b) * p.box_lines));
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      const int64_t b = first + int64_t(s) * step;
+      if (b < p.nbatches) issue(b, s);
+    }
+  }
+
+  const bool active = tid < p.active;
+  const int row_local = tid / p.cpr;
+  const int chunk = tid - row_local * p.cpr;
+
+  int it = 0;
+  for (int64_t batch = first; batch < p.nbatches; batch += step, ++it) {
+    const int s = it % p.stages;
+    const uint32_t parity = uint32_t(it / p.stages) & 1u;
+    if (!mbar_wait(&full[s], parity, DEVERR_TMA_TIMEOUT)) abort_flag = 1;
+    uint8_t* buf = smem + size_t(s) * p.stage_bytes;
+
+    // ---- own line (64 values) from the swizzled stage buffer ------------------
+    float v[64];
+    {
+      const uint32_t line = uint32_t(tid);
+      const uint8_t* lp = buf + line * 128u;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 w = *reinterpret_cast<const uint4*>(lp + ((uint32_t(c) ^ (line & 7u)) << 4));
+        unpack8<BF16>(w, &v[8 * c]);
+      }
+    }
+    stage64<0>(v);
+    if (NST >= 2) stage64<1>(v);
+    if (NST >= 3) stage64<2>(v);
+
+    float amax = 0.0f;
+    float w4[4][16];  // NST == 4 only: [input c][column j] of this thread's block
+    if (NST == 4) {
+      // Swap 16-value blocks among the four threads of a group through this
+      // warp's 4 KB slice of the stage buffer (its own lines, already read).
+      // Row r of the slice is written by lane r; 16-byte chunks are XOR
+      // swizzled with f(r) = ((r&3)<<1) | ((r>>2)&1) so that both the writes
+      // and the transposed reads hit 8 distinct chunk positions per quarter
+      // warp.  Two rounds of 8 columns fit the 4 KB slice.
+      __syncwarp();
+      uint8_t* xb = buf + size_t(warp) * 4096u;
+      const int gq = lane >> 2;
+      const int qd = lane & 3;
+      const uint32_t fw = (uint32_t(qd) << 1) | (uint32_t(gq) & 1u);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const int o = 16 * b + 8 * half + 4 * jj;
+            *reinterpret_cast<float4*>(xb + lane * 128 + ((uint32_t(2 * b + jj) ^ fw) << 4)) =
+                make_float4(v[o], v[o + 1], v[o + 2], v[o + 3]);
+          }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t fr = (uint32_t(c) << 1) | (uint32_t(gq) & 1u);
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const float4 t = *reinterpret_cast<const float4*>(xb + (4 * gq + c) * 128 +
+                                                              ((uint32_t(2 * qd + jj) ^ fr) << 4));
+            const int j = 8 * half + 4 * jj;
+            w4[c][j] = t.x;
+            w4[c][j + 1] = t.y;
+            w4[c][j + 2] = t.z;
+            w4[c][j + 3] = t.w;
+          }
+        }
+        __syncwarp();
+      }
+      // The next TMA into this slot must not overtake these generic accesses.
+      fence_proxy_async_smem();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        bfly4(w4[0][j], w4[1][j], w4[2][j], w4[3][j]);
+        amax = fmaxf(amax, fabsf(w4[0][j]));
+        amax = fmaxf(amax, fabsf(w4[1][j]));
+        amax = fmaxf(amax, fabsf(w4[2][j]));
+        amax = fmaxf(amax, fabsf(w4[3][j]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+
+    // ---- row absmax -----------------------------------------------------------
+    for (int o = 1; o < p.seg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    unsigned* rm = rowmax + (it % 3) * R;
+    if (active && (lane & (p.seg - 1)) == 0) atomicMax(&rm[row_local], __float_as_uint(amax));
+    __syncthreads();
+    if (abort_flag) break;
+
+    // Slot s is free again (every thread has read it): refill it.
+    if (tid == 0) {
+      const int64_t nb = batch + int64_t(p.stages) * step;
+      if (nb < p.nbatches) issue(nb, s);
+    }
+    // Slot (it+2)%3 was last read before the previous barrier and is next
+    // written after the following one.
+    if (tid < R) rowmax[((it + 2) % 3) * R + tid] = 0u;
+
+    const int64_t row = batch * R + row_local;
+    if (active && row < p.M) {
+      const float am = __uint_as_float(rm[row_local]);
+      const float sc = fmaxf(__fdiv_rn(am, kQmaxRoot), 1e-30f);
+      if (chunk == 0) p.scale[row] = sc;
+      const float inv = __fdiv_rn(1.0f, __fmul_rn(sc, kRoot));
+      if (NST == 4) {
+        int8_t* qp = p.q + row * int64_t(p.K) + (chunk >> 2) * 256 + (chunk & 3) * 16;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          uint32_t wd[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            wd[k] = pack4(code_bits(w4[r][4 * k], inv), code_bits(w4[r][4 * k + 1], inv),
+                          code_bits(w4[r][4 * k + 2], inv), code_bits(w4[r][4 * k + 3], inv));
+          *reinterpret_cast<uint4*>(qp + r * 64) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        }
+      } else {
+        int8_t* qp = p.q + row * int64_t(p.K) + chunk * 64;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t wd[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int i = 16 * c + 4 * k;
+            wd[k] = pack4(code_bits(v[i], inv), code_bits(v[i + 1], inv), code_bits(v[i + 2], inv),
+                          code_bits(v[i + 3], inv));
+          }
+          *reinterpret_cast<uint4*>(qp + c * 16) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        }
+      }
+    }
+  }
+
+  // A wait gave up: let the copies still in flight land before the CTA exits.
+  if (abort_flag && tid == 0) {
+    for (int k = it; k < it + p.stages; ++k) {
+      const int64_t b = first + int64_t(k) * step;
+      if (b < p.nbatches) mbar_wait(&full[k % p.stages], uint32_t(k / p.stages) & 1u, DEVERR_TMA_TIMEOUT);
+    }
+  }
+}
+
+}  // namespace tg

@@ -1,0 +1,139 @@
+"""Torch-facing wrappers over the C ABI, plus their ``torch.library`` custom ops.
+
+``rotate_quant`` and ``int8_gemm_dequant`` allocate their outputs with torch's
+caching allocator and enqueue the sm_100a kernels on the current stream of the
+input's device.  They never fall back to another implementation: an input the
+kernels do not handle raises ``ValueError``, a CUDA failure raises
+``TileGenError``.
+
+The same two functions are registered as ``torch.ops.tilegen.rotate_quant`` and
+``torch.ops.tilegen.int8_gemm_dequant`` (with fake implementations, so they
+trace under ``torch.compile``/``torch.export`` as opaque ops).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {
+    torch.float32: _lib.TG_DT_F32,
+    torch.float16: _lib.TG_DT_F16,
+    torch.bfloat16: _lib.TG_DT_BF16,
+}
+_SUPPORTED_GROUPS = (4, 16, 64, 256)
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def _call(func: str, dev: torch.device, *args) -> None:
+    L = _lib.lib()
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    stream = torch.cuda.current_stream(idx).cuda_stream
+    if idx != torch.cuda.current_device():
+        with torch.cuda.device(idx):
+            st = getattr(L, func)(*args, stream)
+    else:
+        st = getattr(L, func)(*args, stream)
+    _lib.check(func, st)
+
+
+def rotate_quant_max_k() -> int:
+    return int(_lib.lib().tg_rotate_quant_max_k())
+
+
+def rotate_quant(x: torch.Tensor, group: int = 256):
+    """Group-Hadamard rotation + row-wise int8 quantisation of ``x [M, K]``.
+
+    Returns ``(q int8 [M, K], scale fp32 [M])``.  ``x`` must be a CUDA fp16/bf16
+    tensor, ``group`` one of 4/16/64/256 and ``K`` a multiple of 256 (at most
+    ``rotate_quant_max_k()``).
+    """
+    if not isinstance(x, torch.Tensor) or not x.is_cuda:
+        raise ValueError("rotate_quant: CUDA tensor required")
+    if x.ndim != 2:
+        raise ValueError(f"rotate_quant: expected 2-D input, got {tuple(x.shape)}")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"rotate_quant: fp16/bf16 input required, got {x.dtype}")
+    if group not in _SUPPORTED_GROUPS:
+        raise ValueError(f"rotate_quant: group must be one of {_SUPPORTED_GROUPS}, got {group}")
+    m, k = x.shape
+    if k % 256:
+        raise ValueError(f"rotate_quant: K={k} must be a multiple of 256")
+    x = _aligned(x)
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m,), dtype=torch.float32, device=x.device)
+    if m:
+        _call("tg_rotate_quant", x.device, x.data_ptr(), _DTYPE_CODE[x.dtype], m, k, int(group),
+              q.data_ptr(), s.data_ptr())
+    return q, s
+
+
+def int8_gemm_dequant(xq: torch.Tensor, xscale: torch.Tensor, wq: torch.Tensor, wscale: torch.Tensor,
+                      bias: torch.Tensor | None, out_dtype: torch.dtype) -> torch.Tensor:
+    """``((float(xq @ wq.T) * xscale[:, None]) * wscale[None, :]) + bias`` as ``out_dtype``.
+
+    ``xq [M, K]`` and ``wq [N, K]`` int8 on the same CUDA device; ``xscale [M]``;
+    ``wscale`` scalar or ``[N]``; ``bias [N]`` fp32/fp16/bf16 or None.
+    """
+    if not (xq.is_cuda and wq.is_cuda):
+        raise ValueError("int8_gemm_dequant: CUDA tensors required")
+    if xq.dtype != torch.int8 or wq.dtype != torch.int8:
+        raise ValueError("int8_gemm_dequant: int8 operands required")
+    if xq.ndim != 2 or wq.ndim != 2 or xq.shape[1] != wq.shape[1]:
+        raise ValueError(f"int8_gemm_dequant: shapes {tuple(xq.shape)} x {tuple(wq.shape)}^T do not match")
+    if out_dtype not in _DTYPE_CODE:
+        raise ValueError(f"int8_gemm_dequant: unsupported out_dtype {out_dtype}")
+    dev = xq.device
+    m, k = xq.shape
+    n = wq.shape[0]
+    xq = _aligned(xq)
+    wq = _aligned(wq.to(dev))
+    xs = xscale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    if xs.numel() != m:
+        raise ValueError(f"int8_gemm_dequant: xscale has {xs.numel()} elements, expected {m}")
+    ws = wscale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    if ws.numel() not in (1, n):
+        raise ValueError(f"weight scale must be scalar or length {n}, got {tuple(wscale.shape)}")
+    b_ptr, b_code = None, _lib.TG_DT_F32
+    if bias is not None:
+        b = bias.to(device=dev).reshape(-1)
+        if b.dtype not in _DTYPE_CODE:
+            b = b.float()
+        b = b.contiguous()
+        if b.numel() != n:
+            raise ValueError(f"int8_gemm_dequant: bias has {b.numel()} elements, expected {n}")
+        bias = b
+        b_ptr, b_code = b.data_ptr(), _DTYPE_CODE[b.dtype]
+    out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    if m:
+        _call("tg_int8_gemm_dequant", dev, xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),
+              ws.numel(), b_ptr, b_code, m, n, k, _DTYPE_CODE[out_dtype], out.data_ptr())
+    return out
+
+
+# ---------------------------------------------------------------- custom ops
+@torch.library.custom_op("tilegen::rotate_quant", mutates_args=())
+def _rotate_quant_op(x: torch.Tensor, group: int) -> tuple[torch.Tensor, torch.Tensor]:
+    return rotate_quant(x, group)
+
+
+@_rotate_quant_op.register_fake
+def _(x, group):
+    return x.new_empty(x.shape, dtype=torch.int8), x.new_empty((x.shape[0],), dtype=torch.float32)
+
+
+@torch.library.custom_op("tilegen::int8_gemm_dequant", mutates_args=())
+def _int8_gemm_dequant_op(xq: torch.Tensor, xscale: torch.Tensor, wq: torch.Tensor, wscale: torch.Tensor,
+                          bias: torch.Tensor | None, out_dtype: torch.dtype) -> torch.Tensor:
+    return int8_gemm_dequant(xq, xscale, wq, wscale, bias, out_dtype)
+
+
+@_int8_gemm_dequant_op.register_fake
+def _(xq, xscale, wq, wscale, bias, out_dtype):
+    return xq.new_empty((xq.shape[0], wq.shape[0]), dtype=out_dtype)

@@ -1,0 +1,65 @@
+"""The C-ABI library loads and exports what include/tilegen_b200.h declares.
+
+No kernel runs here (no GPU): only entry points whose argument checks return
+before any device work are called.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+from tilegen_b200 import _lib
+
+
+def test_library_exports_every_declared_function():
+    names = _lib.declared_functions()
+    assert set(names) >= {"tg_version", "tg_status_string", "tg_rotate_quant", "tg_rotate_quant_max_k",
+                          "tg_int8_gemm_dequant", "tg_device_status"}
+    L = _lib.lib()
+    for n in names:
+        assert hasattr(L, n), n
+
+
+def test_version_and_status_strings():
+    L = _lib.lib()
+    assert L.tg_version() >= 1
+    for code in range(6):
+        assert L.tg_status_string(code)
+    assert L.tg_status_string(0) == b"ok"
+    assert L.tg_rotate_quant_max_k() % 256 == 0
+
+
+def test_argument_checks_return_before_device_work():
+    L = _lib.lib()
+    p = ctypes.c_void_p(16)
+    # unsupported group / K / dtype
+    assert L.tg_rotate_quant(p, _lib.TG_DT_F16, 4, 5120, 128, p, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_rotate_quant(p, _lib.TG_DT_F16, 4, 5000, 256, p, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_rotate_quant(p, _lib.TG_DT_F32, 4, 5120, 256, p, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_rotate_quant(p, _lib.TG_DT_F16, -1, 5120, 256, p, p, None) == _lib.TG_ERR_INVALID_ARG
+    # M == 0 is a no-op
+    assert L.tg_rotate_quant(None, _lib.TG_DT_F16, 0, 5120, 256, None, None, None) == _lib.TG_OK
+    # null pointers with M > 0
+    assert L.tg_rotate_quant(None, _lib.TG_DT_F16, 2, 5120, 256, None, None, None) == _lib.TG_ERR_INVALID_ARG
+    # GEMM: K % 16, N alignment, wscale length, dtype
+    assert L.tg_int8_gemm_dequant(p, p, p, p, 1, None, 0, 4, 64, 24, 1, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_int8_gemm_dequant(p, p, p, p, 1, None, 0, 4, 12, 32, 1, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_int8_gemm_dequant(p, p, p, p, 3, None, 0, 4, 64, 32, 1, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_int8_gemm_dequant(p, p, p, p, 1, None, 0, 4, 64, 32, 7, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_int8_gemm_dequant(None, None, None, None, 1, None, 0, 0, 64, 32, 1, None, None) == _lib.TG_OK
+
+
+def test_check_maps_status_to_exceptions():
+    with pytest.raises(ValueError):
+        _lib.check("tg_rotate_quant", _lib.TG_ERR_UNSUPPORTED)
+    with pytest.raises(_lib.TileGenError):
+        _lib.check("tg_rotate_quant", _lib.TG_ERR_CUDA)
+    _lib.check("x", _lib.TG_OK)
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "nope.so"))
+    with pytest.raises(RuntimeError, match="missing"):
+        _lib.lib()

@@ -1,0 +1,100 @@
+"""The CPU oracle against the reference's own outputs (tests/golden/*.npz).
+
+This pins the oracle before it is trusted as the checker: its rotate+quant must
+reproduce the reference eager path's codes and scales (they agree exactly on
+every fixture case; the north-star tolerance is the bound asserted), and its
+GEMM + dequant must reproduce int8_matmul_dequant_chunked bit for bit.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.conftest import GOLDEN
+
+DT_NAMES = ["float32", "float16", "bfloat16"]
+
+
+def _quant_cases():
+    d = np.load(os.path.join(GOLDEN, "quant.npz"))
+    return d, sorted({f.split("_")[0] for f in d.files})
+
+
+def test_rotate_quant_matches_reference_eager():
+    d, names = _quant_cases()
+    assert len(names) == 7
+    for n in names:
+        m, k, g, dt = (int(v) for v in d[f"{n}_meta"])
+        q, s = oracle.rotate_quant(d[f"{n}_x"], DT_NAMES[dt], g)
+        rq, rs = d[f"{n}_q"], d[f"{n}_scale"]
+        diff = np.abs(q.astype(np.int32) - rq.astype(np.int32))
+        assert diff.max() <= 1 and (diff > 0).mean() <= 1e-3, n
+        assert (np.abs(s - rs) / rs).max() <= 1e-6, n
+        # on these fixtures the agreement is exact
+        assert np.array_equal(q, rq), n
+
+
+def test_weight_quant_matches_reference():
+    d = np.load(os.path.join(GOLDEN, "weight.npz"))
+    q, s = oracle.rotate_quant(d["w"], "float32", 256)
+    assert np.array_equal(q, d["wq"])
+    assert (np.abs(s - d["wscale"]) / d["wscale"]).max() <= 1e-6
+
+
+def test_gemm_dequant_bit_exact_vs_reference():
+    d = np.load(os.path.join(GOLDEN, "gemm.npz"))
+    for n in "abcd":
+        m, nn, k, od, has_bias, scalar = (int(v) for v in d[f"{n}_meta"])
+        y = oracle.int8_gemm_dequant(d[f"{n}_xq"], d[f"{n}_xscale"], d[f"{n}_wq"], d[f"{n}_wscale"],
+                                     d[f"{n}_bias"] if has_bias else None, DT_NAMES[od])
+        assert np.array_equal(y.view(np.uint8), d[f"{n}_y"].view(np.uint8)), n
+
+
+def test_config1_end_to_end():
+    """The CPU reference workload: same seeded inputs, scales and head outputs."""
+    from tilegen_b200.synthetic import gaussian_weight, outlier_activations
+
+    g = np.load(os.path.join(GOLDEN, "config1.npz"))
+    x = outlier_activations(256, 5120, seed=0, dtype=torch.float32)
+    w = gaussian_weight(5120, 5120, seed=0)
+    sha = lambda t: hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+    assert sha(x) == str(g["x_sha"]) and sha(w) == str(g["w_sha"]), "seeded inputs changed"
+    xq, xs = oracle.rotate_quant(x.numpy(), "float32", 256)
+    wq, ws = oracle.rotate_quant(w.numpy(), "float32", 256)
+    assert (np.abs(xs - g["xscale"]) / g["xscale"]).max() <= 1e-5
+    assert (np.abs(ws - g["wscale"]) / g["wscale"]).max() <= 1e-5
+    dq = np.abs(xq[:8].astype(int) - g["xq_head"].astype(int))
+    assert dq.max() <= 1 and (dq > 0).mean() <= 1e-3
+    y = oracle.int8_gemm_dequant(xq[:8], xs[:8], wq, ws, None, "float32")
+    rel = np.linalg.norm(y - g["y_head"]) / np.linalg.norm(g["y_head"])
+    assert rel <= 1e-2
+    assert float(g["rel_vs_dense"]) < 2e-2
+
+
+def test_planted_mistake_is_caught():
+    """A wrong butterfly sign (planted in a Python copy of the oracle's math) changes the codes."""
+    x = np.random.default_rng(0).standard_normal((2, 256)).astype(np.float32)
+    q, _ = oracle.rotate_quant(x, "float32", 256)
+    y = x.copy().reshape(2, 256)
+    for st in range(4):
+        s = 1 << (2 * st)
+        for b in range(64):
+            base = (b // s) * 4 * s + b % s
+            a0, a1, a2, a3 = (y[:, base + i * s].copy() for i in range(4))
+            y[:, base], y[:, base + s] = a0 + a1 + a2 - a3, a0 + a1 - a2 + a3
+            y[:, base + 2 * s], y[:, base + 3 * s] = a0 - a1 + a2 + a3, a0 + a1 + a2 + a3  # planted: -a0 -> +a0
+    scale = np.maximum(np.abs(y).max(1) / 2032, 1e-30)
+    bad = np.clip(np.rint(y / (16 * scale[:, None])), -128, 127).astype(np.int8)
+    assert not np.array_equal(bad, q)
+
+
+def test_rejects_bad_groups():
+    with pytest.raises(ValueError):
+        oracle.rotate_quant(np.zeros((1, 256), np.float32), "float32", 128)
+    with pytest.raises(ValueError):
+        oracle.rotate_quant(np.zeros((1, 320), np.float32), "float32", 256)

@@ -1,0 +1,448 @@
+"""Benchmark of the int8_convrot linear (rotate+quant -> fused INT8 GEMM + dequant).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tilegen|reference]
+
+Workload (one step): the qkv_proj linear of a 14B-class video DiT block at
+M=4096 tokens per GPU: x fp16 [4096, 5120] ~ N(0,1) with 1 % outlier channels
+x30, W int8 [15360, 5120] (a N(0,0.02) weight quantised by the same kernel),
+group 256, output fp16 [4096, 15360].  Synthetic, seeded data.
+
+Metric: linear time in microseconds (lower is better).  With N ranks each rank
+runs its own 4096-row linear (rows shard with no collective), so the job
+processes N linears per step and ``value`` = max-over-ranks time / (N * steps):
+microseconds per 4096-row linear for the whole job.  L2 is flushed (a 256 MiB
+write) before every timed step; each step is timed with CUDA events on the
+launching stream.
+
+The JSON line also carries: the roofline of the dominant kernel (the GEMM,
+tensor-bound) and of the quantiser (HBM-bound), the cuBLAS bf16 F.linear time
+of the same shape and the speedup over it, an end-to-end number through the
+public API with host buffers, the CPU baseline (the oracle port on the host
+cores, a bounded sample), sampled SM clocks, and (N=1) the four DiT shapes.
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+oracle port, all host threads) on the same workload; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+M_PER_RANK = 4096
+GROUP = 256
+SHAPE = ("qkv_proj", 5120, 15360)
+NOMINAL_INT8_TOPS = 4500.0
+BASELINE_QKV_US = 10550.0  # RTX 2080 Ti, tilegen FHT int8_convrot qkv_proj, README.md:9
+
+
+def _peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def _workload_desc():
+    name, k, n = SHAPE
+    return (f"{name} int8_convrot linear: x fp16 [{M_PER_RANK},{k}] N(0,1) with 1% outlier channels x30, "
+            f"W int8 [{n},{k}] per-channel fp32 scales, group {GROUP}, out fp16 [{M_PER_RANK},{n}]")
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+        if 0 <= gpu_index < len(vis) and vis[gpu_index].strip().isdigit():
+            gpu_index = int(vis[gpu_index])
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------ helpers
+def _setup_dist(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        if args.impl == "tilegen":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+class CpuLinear:
+    """The reference algorithm on the host cores (the C oracle port, all threads).
+
+    The weight is quantised once at set-up (it is offline in the reference too);
+    ``time_rows(m)`` times rotate+quant and GEMM+dequant of ``m`` activation rows.
+    """
+
+    def __init__(self, k: int, n: int):
+        import torch
+
+        import oracle
+        from tilegen_b200.synthetic import gaussian_weight, outlier_activations
+
+        self.oracle = oracle
+        oracle.set_num_threads(os.cpu_count() or 1)
+        self.x = outlier_activations(M_PER_RANK, k, seed=0, dtype=torch.float16).view(torch.int16).numpy()
+        self.wq, self.ws = oracle.rotate_quant(gaussian_weight(n, k, seed=0).numpy(), "float32", GROUP)
+        self.threads = oracle.num_threads()
+
+    def time_rows(self, m: int) -> float:
+        t0 = time.perf_counter()
+        xq, xs = self.oracle.rotate_quant(self.x[:m], "float16", GROUP)
+        self.oracle.int8_gemm_dequant(xq, xs, self.wq, self.ws, None, "float16")
+        return time.perf_counter() - t0
+
+    def rows_for(self, seconds: float) -> int:
+        """Row count whose sample takes about ``seconds`` (at least 8, at most all)."""
+        t8 = self.time_rows(8)
+        return int(max(8, min(M_PER_RANK, 8 * seconds / max(t8, 1e-4))))
+
+
+def _cpu_baseline_us(k, n, budget_s=10.0):
+    """Oracle time for one full 4096-row linear, scaled from a bounded row sample."""
+    cpu = CpuLinear(k, n)
+    m = cpu.rows_for(budget_s)
+    dt = cpu.time_rows(m)
+    return dt / m * M_PER_RANK * 1e6, cpu.threads, f"{m} of {M_PER_RANK} rows (rotate+quant and GEMM+dequant), scaled"
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    name, k, n = SHAPE
+    cpu = CpuLinear(k, n)
+    # every step times the same bounded row sample; the whole run stays near 90 s
+    m = cpu.rows_for(90.0 / max(1, args.steps + args.warmup))
+    for _ in range(args.warmup):
+        cpu.time_rows(m)
+    per_step = [cpu.time_rows(m) / m * M_PER_RANK * 1e6 for _ in range(args.steps)]
+    thr = cpu.threads
+    sample = f"{m} of {M_PER_RANK} rows per step (rotate+quant and GEMM+dequant), scaled to {M_PER_RANK}"
+    value = statistics.mean(per_step)
+    line = {
+        "metric": "int8_convrot linear us (M=4096) & speedup vs bf16 cuBLAS; quantizer HBM GB/s",
+        "value": value, "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": value / 1e3, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic", "impl": "reference",
+        "config": {"workload": _workload_desc(), "M": M_PER_RANK, "K": k, "N": n, "group": GROUP,
+                   "parallelism": "rank 0 host cores"},
+        "cpu_baseline": {"value": value, "unit": "us", "cores": thr, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ tilegen arm
+def _time_steps(fn, steps, flush, stream, marks=1):
+    """Run ``fn(events)`` ``steps`` times, flushing L2 before each; per-step event times (ms)."""
+    import torch
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(marks + 1)] for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        fn(evs[i])
+    torch.cuda.synchronize()
+    return [[evs[i][j].elapsed_time(evs[i][j + 1]) for j in range(marks)] for i in range(steps)]
+
+
+def _bf16_linear_us(x16, w_bf16, steps, flush, stream):
+    import torch
+    import torch.nn.functional as F
+
+    xb = x16.to(torch.bfloat16)
+
+    def f(e):
+        e[0].record(stream)
+        F.linear(xb, w_bf16)
+        e[1].record(stream)
+
+    for _ in range(3):
+        f([torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)])
+    t = _time_steps(f, steps, flush, stream)
+    return statistics.mean(r[0] for r in t) * 1e3
+
+
+def _int_mm_tops(dev):
+    """cuBLASLt int8 GEMM throughput (torch._int_mm, 8192^3, best of 10) on this GPU."""
+    import torch
+
+    a = torch.randint(-128, 128, (8192, 8192), dtype=torch.int8, device=dev)
+    b = torch.randint(-128, 128, (8192, 8192), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a, b.t())
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._int_mm(a, b.t())
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e))
+    return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
+
+
+def _shape_table(dev, flush, stream, iters=20):
+    import torch
+
+    from tilegen_b200 import ops
+    from tilegen_b200.synthetic import DIT_SHAPES, dit_activations, gaussian_weight
+
+    rows = []
+    for name, k, n in DIT_SHAPES:
+        x = dit_activations(name, M_PER_RANK, seed=0, dtype=torch.float16, device=dev)
+        w = gaussian_weight(n, k, seed=1, dtype=torch.bfloat16, device=dev)
+        wq, ws = ops.rotate_quant(w, GROUP)
+
+        def f(e):
+            e[0].record(stream)
+            xq, xs = ops.rotate_quant(x, GROUP)
+            e[1].record(stream)
+            ops.int8_gemm_dequant(xq, xs, wq, ws, None, torch.float16)
+            e[2].record(stream)
+
+        for _ in range(3):
+            f([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+        t = _time_steps(f, iters, flush, stream, marks=2)
+        tq = statistics.mean(r[0] for r in t) * 1e3
+        tg = statistics.mean(r[1] for r in t) * 1e3
+        tb = _bf16_linear_us(x, w, iters, flush, stream)
+        qbytes = M_PER_RANK * k * 3 + 4 * M_PER_RANK
+        rows.append({"shape": name, "K": k, "N": n, "int8_linear_us": round(tq + tg, 2), "quant_us": round(tq, 2),
+                     "gemm_us": round(tg, 2), "bf16_cublas_us": round(tb, 2), "speedup_vs_bf16": round(tb / (tq + tg), 3),
+                     "quant_gbs": round(qbytes / (tq * 1e-6) / 1e9, 1),
+                     "gemm_tops": round(2 * M_PER_RANK * n * k / (tg * 1e-6) / 1e12, 1)})
+        del x, w, wq, ws
+    return rows
+
+
+def run_tilegen(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = _setup_dist(args)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from tilegen.kernels.int8_convrot import quantize_convrot
+    from tilegen.quant.int8_ops import int8_matmul_dequant_chunked
+    from tilegen_b200 import _lib, ops
+    from tilegen_b200.synthetic import gaussian_weight, outlier_activations
+
+    peaks, peak_kind = _peaks()
+    name, k, n = SHAPE
+    m = M_PER_RANK
+    x = outlier_activations(m, k, seed=rank, dtype=torch.float16, device=dev)
+    w = gaussian_weight(n, k, seed=1000, dtype=torch.bfloat16, device=dev)
+    wq, ws = ops.rotate_quant(w, GROUP)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(e):
+        e[0].record(stream)
+        xq, xs = ops.rotate_quant(x, GROUP)
+        e[1].record(stream)
+        ops.int8_gemm_dequant(xq, xs, wq, ws, None, torch.float16)
+        e[2].record(stream)
+
+    for _ in range(max(3, args.warmup)):
+        step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    with ClockSampler(local) as clk:
+        t = _time_steps(step, args.steps, flush, stream, marks=2)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    if world > 1:
+        dist.barrier()
+    clocks = clk.summary()
+    tq = [r[0] for r in t]
+    tg = [r[1] for r in t]
+    total_ms = sum(a + b for a, b in zip(tq, tg))
+    tot = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    max_total_ms = float(tot.item())
+    value_us = max_total_ms * 1e3 / (world * args.steps)
+
+    if args.quick:
+        if world > 1:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"quick": True, "value_us": round(value_us, 3), "quant_us": round(statistics.mean(tq) * 1e3, 2),
+                              "gemm_us": round(statistics.mean(tg) * 1e3, 2), "clocks": clocks}), flush=True)
+        return
+
+    # ---- end to end through the public API, host buffers, copies timed ----
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((m, n), dtype=torch.float16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step(e):
+        e[0].record(stream)
+        x_dev.copy_(x_host, non_blocking=True)
+        xq, xs = quantize_convrot(x_dev, GROUP, backend="fht")
+        y = int8_matmul_dequant_chunked(xq, xs, wq, ws, None, torch.float16)
+        out_host.copy_(y, non_blocking=True)
+        e[1].record(stream)
+
+    for _ in range(3):
+        e2e_step([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+    if world > 1:
+        dist.barrier()
+    te = _time_steps(e2e_step, max(3, min(args.steps, 50)), flush, stream)
+    e2e_total = torch.tensor([sum(r[0] for r in te)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
+    e2e_us = float(e2e_total.item()) * 1e3 / (world * len(te))
+
+    # ---- comparators ----
+    bf16_us = _bf16_linear_us(x, w, max(5, min(args.steps, 50)), flush, stream)
+    int8_lib_tops = _int_mm_tops(dev)
+    status = _lib.device_status(local)
+
+    shapes = cpu = None
+    if world == 1:
+        shapes = _shape_table(dev, flush, stream)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu_us, cores, sample = _cpu_baseline_us(k, n)
+        cpu = {"value": round(cpu_us, 1), "unit": "us", "cores": cores, "kind": "port", "sample": sample}
+
+    if world > 1:
+        if rank == 0:
+            pass
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    gemm_ms = statistics.mean(tg)
+    quant_ms = statistics.mean(tq)
+    gemm_tops = 2 * m * n * k / (gemm_ms * 1e-3) / 1e12
+    quant_bytes = m * k * 2 + m * k + 4 * m
+    quant_gbs = quant_bytes / (quant_ms * 1e-3) / 1e9
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    lin_us = (quant_ms + gemm_ms) * 1e3
+    line = {
+        "metric": "int8_convrot linear us (M=4096) & speedup vs bf16 cuBLAS; quantizer HBM GB/s",
+        "value": round(value_us, 3), "unit": "us", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": round(max_total_ms / args.steps, 5),
+        "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": round(value_us / BASELINE_QKV_US, 5),
+        "vs_baseline_ref": "tilegen FHT int8_convrot qkv_proj on RTX 2080 Ti, 10.55 ms (README.md:9)",
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": _workload_desc(), "M_per_gpu": m, "K": k, "N": n, "group": GROUP,
+                   "parallelism": f"rows x {world} (no collective)",
+                   "l2": "flushed before every timed step (256 MiB write)"},
+        "speedup_vs_bf16_cublas": round(bf16_us / lin_us, 3), "bf16_cublas_us": round(bf16_us, 2),
+        "quant_us": round(quant_ms * 1e3, 2), "gemm_us": round(gemm_ms * 1e3, 2),
+        "roofline": {"bound": "tensor", "kernel": "gemm_i8_dequant_kernel", "achieved": round(gemm_tops, 1),
+                     "peak": round(int8_peak, 1), "unit": "TOP/s", "frac": round(gemm_tops / int8_peak, 4),
+                     "peak_source": f"2 x {peak_kind} bf16 cuBLAS burst (dense int8 = 2 x dense bf16)",
+                     "traffic": None, "algorithmic_ops_per_launch": 2 * m * n * k,
+                     "vs_cublaslt_int8_tops": round(int8_lib_tops, 1),
+                     "vs_nominal_int8": round(gemm_tops / NOMINAL_INT8_TOPS, 4)},
+        "quant_roofline": {"bound": "hbm", "kernel": "rotquant_kernel", "achieved": round(quant_gbs, 1),
+                           "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(quant_gbs / peaks["hbm_gbs"], 4),
+                           "peak_source": peak_kind, "algorithmic_bytes_per_launch": quant_bytes, "traffic": None},
+        "e2e": {"value": round(e2e_us, 2), "unit": "us", "h2d_bytes_per_step": x.numel() * 2,
+                "d2h_bytes_per_step": m * n * 2,
+                "path": "pinned host x -> tilegen.kernels.quantize_convrot -> tilegen.quant.int8_matmul_dequant_chunked -> pinned host out"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+        "device_status": status,
+        "wall_s_timed_region": round(wall, 3),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if shapes is not None:
+        line["dit_shapes"] = shapes
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("tilegen", "reference"), default="tilegen")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--quick", action="store_true",
+                    help="only the timed loop (no e2e, comparators, shape table or CPU baseline); for profiling")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_tilegen(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -85,6 +85,21 @@ int tg_int8_gemm_dequant(const int8_t *xq, const float *xscale, const int8_t *wq
                          int64_t K, int out_dtype, void *out, void *stream);
 
 /*
+ * Tile width (UMMA N: 256, 224, 192, 160 or 128) tg_int8_gemm_dequant will use
+ * for an M x N problem on the current device, or -1 if no device is usable.
+ * The width minimises (persistent waves) x (tile cost) over the SMs.  No
+ * reference counterpart (cuBLASLt picked its own tiles).
+ */
+int tg_gemm_tile_width(int64_t M, int64_t N);
+
+/*
+ * Force the GEMM tile width for every later call in this process (0 restores
+ * the automatic choice).  For tests and tuning; returns TG_ERR_INVALID_ARG for
+ * a width the library was not built with.
+ */
+int tg_set_gemm_tile_width(int bn);
+
+/*
  * Read (and optionally clear) the device status word of `device`, which
  * kernels set when a bounded wait expires.  Synchronises the device.
  * *bits receives the raw word (0 = healthy); returns TG_ERR_DEVICE_TIMEOUT when

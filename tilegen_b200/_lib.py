@@ -99,6 +99,10 @@ def lib() -> ctypes.CDLL:
         L.tg_rotate_quant_max_k.restype = i64
         L.tg_int8_gemm_dequant.argtypes = [p, p, p, p, i64, p, i32, i64, i64, i64, i32, p, p]
         L.tg_int8_gemm_dequant.restype = i32
+        L.tg_gemm_tile_width.argtypes = [i64, i64]
+        L.tg_gemm_tile_width.restype = i32
+        L.tg_set_gemm_tile_width.argtypes = [i32]
+        L.tg_set_gemm_tile_width.restype = i32
         L.tg_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint32), i32]
         L.tg_device_status.restype = i32
         _lib = L

@@ -13,6 +13,7 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr int64_t kRotQuantMaxK = 32768;
+constexpr int kRotQuantRegs = 96;  // __maxnreg__ of rotquant_kernel
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -161,7 +162,12 @@ int tg_rotate_quant(const void* x, int x_dtype, int64_t M, int64_t K, int group,
       }
   }
   const uint32_t stage_bytes = uint32_t(threads) * 128u;
-  int stages = int((110u * 1024u) / stage_bytes);
+  // Ring depth: as deep as possible (up to 4) while the CTAs that the register
+  // budget allows per SM (96 registers a thread) still fit in shared memory.
+  int ctas = 65536 / (threads * kRotQuantRegs);
+  ctas = ctas < 1 ? 1 : ctas;
+  const uint32_t per_cta = 232448u / uint32_t(ctas) - 2048u - 1024u - uint32_t(3 * R) * 4u;
+  int stages = int(per_cta / stage_bytes);
   stages = stages < 2 ? 2 : (stages > 4 ? 4 : stages);
   const uint32_t smem = 1024u + uint32_t(stages) * stage_bytes + uint32_t(stages) * 8u + uint32_t(3 * R) * 4u;
 
@@ -207,16 +213,55 @@ int tg_rotate_quant(const void* x, int x_dtype, int64_t M, int64_t K, int group,
 
 namespace {
 
-template <int OUT, bool HAS_BIAS>
+template <int BN, int OUT, bool HAS_BIAS>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const tg::GemmParams& p,
                   int dev, int sms, cudaStream_t st) {
   static uint32_t attr_done[kMaxDevices];
-  auto kern = tg::gemm_i8_dequant_kernel<OUT, HAS_BIAS>;
-  if (!ensure_smem_attr(kern, dev, tg::gemm::SMEM_BYTES, attr_done)) return TG_ERR_CUDA;
+  constexpr uint32_t smem = tg::gemm::smem_bytes<BN>();
+  auto kern = tg::gemm_i8_dequant_kernel<BN, OUT, HAS_BIAS>;
+  if (!ensure_smem_attr(kern, dev, smem, attr_done)) return TG_ERR_CUDA;
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sms ? tiles : sms;
-  kern<<<dim3(unsigned(grid)), dim3(tg::gemm::THREADS), tg::gemm::SMEM_BYTES, st>>>(ta, tb, to, p);
+  kern<<<dim3(unsigned(grid)), dim3(tg::gemm::THREADS), smem, st>>>(ta, tb, to, p);
   return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
+}
+
+template <int BN>
+int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const tg::GemmParams& p,
+                   int out_dtype, bool has_bias, int dev, int sms, cudaStream_t st) {
+  switch (out_dtype) {
+    case TG_DT_F32: return has_bias ? launch_gemm_t<BN, 0, true>(ta, tb, to, p, dev, sms, st)
+                                    : launch_gemm_t<BN, 0, false>(ta, tb, to, p, dev, sms, st);
+    case TG_DT_F16: return has_bias ? launch_gemm_t<BN, 1, true>(ta, tb, to, p, dev, sms, st)
+                                    : launch_gemm_t<BN, 1, false>(ta, tb, to, p, dev, sms, st);
+    default: return has_bias ? launch_gemm_t<BN, 2, true>(ta, tb, to, p, dev, sms, st)
+                             : launch_gemm_t<BN, 2, false>(ta, tb, to, p, dev, sms, st);
+  }
+}
+
+// Tile width for an M x N problem on `sms` SMs: the persistent grid runs
+// ceil(tiles / sms) waves of tiles costing about (BN + kTileOverhead) column
+// steps each, so pick the width that minimises waves * (BN + overhead).
+constexpr int kGemmWidths[] = {256, 224, 192, 160, 128};
+constexpr int kTileOverhead = 32;
+
+int g_forced_bn = 0;  // tg_set_gemm_tile_width(); 0 = pick by the cost model
+
+int pick_gemm_bn(int64_t M, int64_t N, int sms) {
+  if (g_forced_bn) return g_forced_bn;
+  const int64_t mt = (M + tg::gemm::BM - 1) / tg::gemm::BM;
+  int best = 256;
+  int64_t best_cost = -1;
+  for (int bn : kGemmWidths) {
+    const int64_t tiles = mt * ((N + bn - 1) / bn);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const int64_t cost = waves * (bn + kTileOverhead);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
 }
 
 }  // namespace
@@ -245,18 +290,21 @@ int tg_int8_gemm_dequant(const int8_t* xq, const float* xscale, const int8_t* wq
   DeviceInfo info;
   if (!current_device(&dev, &info)) return TG_ERR_CUDA;
 
+  const int bn = pick_gemm_bn(M, N, info.sms);
+  const int ch_bytes = (bn * esz) % 128 == 0 ? 128 : 64;  // epilogue chunk row bytes (kernel's CH_BYTES)
+
   CUtensorMap ta, tb, to;
   if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, uint64_t(K), uint64_t(M), uint64_t(K), BK, BM,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return TG_ERR_CUDA;
-  if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, uint64_t(K), uint64_t(N), uint64_t(K), BK, BN,
-                    CU_TENSOR_MAP_SWIZZLE_128B))
+  if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, uint64_t(K), uint64_t(N), uint64_t(K), BK,
+                    uint32_t(bn), CU_TENSOR_MAP_SWIZZLE_128B))
     return TG_ERR_CUDA;
   const CUtensorMapDataType odt = out_dtype == TG_DT_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                   : out_dtype == TG_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  if (!make_tmap_2d(&to, odt, out, uint64_t(N), uint64_t(M), uint64_t(N) * esz, uint32_t(128 / esz), 32,
-                    CU_TENSOR_MAP_SWIZZLE_128B))
+  if (!make_tmap_2d(&to, odt, out, uint64_t(N), uint64_t(M), uint64_t(N) * esz, uint32_t(ch_bytes / esz), 32,
+                    ch_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
     return TG_ERR_CUDA;
 
   tg::GemmParams p;
@@ -269,19 +317,38 @@ int tg_int8_gemm_dequant(const int8_t* xq, const float* xscale, const int8_t* wq
   p.N = int(N);
   p.K = int(K);
   p.m_tiles = int((M + BM - 1) / BM);
-  p.n_tiles = int((N + BN - 1) / BN);
+  p.n_tiles = int((N + bn - 1) / bn);
   p.k_blocks = int((K + BK - 1) / BK);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool hb = bias != nullptr;
-  switch (out_dtype) {
-    case TG_DT_F32: return hb ? launch_gemm_t<0, true>(ta, tb, to, p, dev, info.sms, st)
-                              : launch_gemm_t<0, false>(ta, tb, to, p, dev, info.sms, st);
-    case TG_DT_F16: return hb ? launch_gemm_t<1, true>(ta, tb, to, p, dev, info.sms, st)
-                              : launch_gemm_t<1, false>(ta, tb, to, p, dev, info.sms, st);
-    default: return hb ? launch_gemm_t<2, true>(ta, tb, to, p, dev, info.sms, st)
-                       : launch_gemm_t<2, false>(ta, tb, to, p, dev, info.sms, st);
+  switch (bn) {
+    case 224: return launch_gemm_bn<224>(ta, tb, to, p, out_dtype, hb, dev, info.sms, st);
+    case 192: return launch_gemm_bn<192>(ta, tb, to, p, out_dtype, hb, dev, info.sms, st);
+    case 160: return launch_gemm_bn<160>(ta, tb, to, p, out_dtype, hb, dev, info.sms, st);
+    case 128: return launch_gemm_bn<128>(ta, tb, to, p, out_dtype, hb, dev, info.sms, st);
+    default: return launch_gemm_bn<256>(ta, tb, to, p, out_dtype, hb, dev, info.sms, st);
   }
+}
+
+int tg_set_gemm_tile_width(int bn) {
+  if (bn == 0) {
+    g_forced_bn = 0;
+    return TG_OK;
+  }
+  for (int w : kGemmWidths)
+    if (w == bn) {
+      g_forced_bn = bn;
+      return TG_OK;
+    }
+  return TG_ERR_INVALID_ARG;
+}
+
+int tg_gemm_tile_width(int64_t M, int64_t N) {
+  int dev;
+  DeviceInfo info;
+  if (!current_device(&dev, &info)) return -1;
+  return pick_gemm_bn(M, N, info.sms);
 }
 
 int tg_device_status(int device, uint32_t* bits, int clear) {

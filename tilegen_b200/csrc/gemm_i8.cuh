@@ -28,21 +28,26 @@ namespace tg {
 
 namespace gemm {
 constexpr int BM = 128;               // rows of xq per tile (UMMA M)
-constexpr int BN = 256;               // rows of wq per tile (UMMA N)
+constexpr int BN_MAX = 256;           // widest tile (rows of wq per tile, UMMA N)
 constexpr int BK = 128;               // bytes (= int8 elements) of K per k-block
 constexpr int UK = 32;                // K per tcgen05.mma kind::i8
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK;      // 16 KB
-constexpr int B_BYTES = BN * BK;      // 32 KB
 constexpr int OUT_BYTES = 32 * 128;   // one 32-row x 128-byte epilogue chunk per warp
 constexpr int THREADS = 192;
-constexpr int TMEM_COLS = 512;        // two BN-wide int32 accumulators
-constexpr uint32_t SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 4 * OUT_BYTES + 1024;
+constexpr int TMEM_COLS = 512;        // two accumulators, at columns 0 and 256
+
+template <int BN>
+__host__ __device__ constexpr uint32_t smem_bytes() {
+  return STAGES * (A_BYTES + BN * BK) + 4 * OUT_BYTES + 1024;
+}
 
 // tcgen05 instruction descriptor: D=S32 (bits 4-5 = 2), A=B=S8 (bits 7-9 and
 // 10-12 = 1), both K-major, N>>3 at bits 17-22, M>>4 at bits 24-28.
-constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
-                           (uint32_t(BM >> 4) << 24);
+template <int BN>
+__host__ __device__ constexpr uint32_t idesc() {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+}
 
 // Shared-memory matrix descriptor for a K-major operand tile stored as rows
 // of 128 bytes in the 128-byte swizzle: start address >> 4, leading byte
@@ -64,15 +69,22 @@ struct GemmParams {
   int m_tiles, n_tiles, k_blocks;
 };
 
-// OUT: 0 fp32, 1 fp16, 2 bf16 (tg_dtype codes)
-template <int OUT, bool HAS_BIAS>
+// BN: tile width (a multiple of 32, at most 256); OUT: 0 fp32, 1 fp16, 2 bf16
+// (tg_dtype codes).
+template <int BN, int OUT, bool HAS_BIAS>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_i8_dequant_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                            const __grid_constant__ CUtensorMap tma_out, const GemmParams p) {
   using namespace gemm;
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= BN_MAX, "tile width");
   constexpr int ESZ = OUT == 0 ? 4 : 2;
-  constexpr int CH = 128 / ESZ;        // output columns per epilogue chunk (128 bytes)
+  // Epilogue chunk: 128-byte rows (128-byte swizzle) when the tile width
+  // allows, else 64-byte rows (64-byte swizzle).
+  constexpr int CH_BYTES = (BN * ESZ) % 128 == 0 ? 128 : 64;
+  constexpr int CH = CH_BYTES / ESZ;   // output columns per epilogue chunk
   constexpr int NCH = BN / CH;         // chunks per tile
+  constexpr int B_BYTES = BN * BK;
+  constexpr uint32_t IDESC = idesc<BN>();
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -87,8 +99,8 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   __shared__ __align__(8) uint64_t tempty_bar[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
-  __shared__ __align__(16) float col_ws[BN];
-  __shared__ __align__(16) float col_bias[BN];
+  __shared__ __align__(16) float col_ws[BN_MAX];
+  __shared__ __align__(16) float col_bias[BN_MAX];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -165,7 +177,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         const uint32_t acc_phase = uint32_t(local >> 1) & 1u;
         if (!wait(&tempty_bar[ab], acc_phase ^ 1u, DEVERR_PIPE_TIMEOUT)) goto done;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(ab * BN);
+        const uint32_t d_tmem = tmem_base + uint32_t(ab * BN_MAX);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!wait(&full_bar[stage], phase, DEVERR_TMA_TIMEOUT)) goto done;
           tc_fence_after();
@@ -218,7 +230,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 
       const int row = m0 + quarter * 32 + lane;
       const float xs = row < p.M ? p.xscale[row] : 0.0f;
-      const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(ab * BN);
+      const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(ab * BN_MAX);
 
 #pragma unroll 1
       for (int ch = 0; ch < NCH; ++ch) {
@@ -239,9 +251,9 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 
         const float* cws = col_ws + ch * CH;
         const float* cbs = col_bias + ch * CH;
-        uint8_t* srow = sbuf + lane * 128;
+        uint8_t* srow = sbuf + lane * CH_BYTES;
 #pragma unroll
-        for (int c16 = 0; c16 < 8; ++c16) {  // 16 output bytes per step
+        for (int c16 = 0; c16 < CH_BYTES / 16; ++c16) {  // 16 output bytes per step
           uint32_t pk[4];
           constexpr int PER = 16 / ESZ;       // values per 16 bytes
 #pragma unroll
@@ -276,8 +288,10 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
               pk[e / 2 + 1] = *reinterpret_cast<uint32_t*>(&h1);
             }
           }
-          *reinterpret_cast<uint4*>(srow + ((uint32_t(c16) ^ uint32_t(lane & 7)) << 4)) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          // 128-byte swizzle: chunk ^= row & 7; 64-byte swizzle: chunk ^= (row >> 1) & 3.
+          const uint32_t pc = CH_BYTES == 128 ? (uint32_t(c16) ^ uint32_t(lane & 7))
+                                              : (uint32_t(c16) ^ uint32_t((lane >> 1) & 3));
+          *reinterpret_cast<uint4*>(srow + (pc << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
         fence_proxy_async_smem();
         __syncwarp();

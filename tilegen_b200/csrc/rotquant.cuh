@@ -63,56 +63,110 @@ __device__ __forceinline__ void bfly4(float& a0, float& a1, float& a2, float& a3
   a3 = y3;
 }
 
-// Radix-4 stage ST (stride 4^ST) over 64 values held in registers.
-template <int ST>
-__device__ __forceinline__ void stage64(float (&v)[64]) {
-  constexpr int stride = 1 << (2 * ST);
+// Paired fp32 arithmetic (sm_100 add/sub/mul.rn.f32x2): two independent IEEE
+// round-to-nearest operations per instruction, the same results as two scalar
+// operations.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+// bfly4 on two independent butterflies at once (lanes .x and .y).
+__device__ __forceinline__ void bfly4x2(float2& a0, float2& a1, float2& a2, float2& a3) {
+  const float2 s = add2(a0, a1);
+  const float2 d = sub2(a0, a1);
+  const float2 y0 = sub2(add2(s, a2), a3);
+  const float2 y1 = add2(sub2(s, a2), a3);
+  const float2 y2 = add2(add2(d, a2), a3);
+  const float2 y3 = add2(sub2(a2, d), a3);
+  a0 = y0;
+  a1 = y1;
+  a2 = y2;
+  a3 = y3;
+}
+
+// max(m, |a|, |b|) in one three-input max; NaN operands are ignored as by fmaxf.
+__device__ __forceinline__ float absmax3(float m, float a, float b) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(m), "f"(fabsf(a)), "f"(fabsf(b)));
+  return r;
+}
+
+// The thread's 64 values are held as 32 pairs vp[k] = (v[2k], v[2k+1]).
+// Stage 0 (stride 1) pairs two inputs of one butterfly, so it runs scalar;
+// stages 1 and 2 (strides 4 and 16) pair the butterflies at positions p and
+// p+1, which are independent and identical, so they run on f32x2.
+__device__ __forceinline__ void stage0_64(float2 (&vp)[32]) {
 #pragma unroll
-  for (int b = 0; b < 16; ++b) {
-    const int low = b % stride;
-    const int high = b / stride;
-    const int base = high * 4 * stride + low;
-    bfly4(v[base], v[base + stride], v[base + 2 * stride], v[base + 3 * stride]);
-  }
+  for (int h = 0; h < 16; ++h) bfly4(vp[2 * h].x, vp[2 * h].y, vp[2 * h + 1].x, vp[2 * h + 1].y);
+}
+
+__device__ __forceinline__ void stage1_64(float2 (&vp)[32]) {
+#pragma unroll
+  for (int h = 0; h < 4; ++h)
+#pragma unroll
+    for (int u = 0; u < 2; ++u) bfly4x2(vp[8 * h + u], vp[8 * h + 2 + u], vp[8 * h + 4 + u], vp[8 * h + 6 + u]);
+}
+
+__device__ __forceinline__ void stage2_64(float2 (&vp)[32]) {
+#pragma unroll
+  for (int l = 0; l < 8; ++l) bfly4x2(vp[l], vp[l + 8], vp[l + 16], vp[l + 24]);
 }
 
 template <bool BF16>
-__device__ __forceinline__ void unpack8(const uint4 w, float* f) {
+__device__ __forceinline__ void unpack8(const uint4 w, float2* f) {
   const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     if (BF16) {
-      f[2 * i] = __uint_as_float(u[i] << 16);
-      f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+      f[i] = make_float2(__uint_as_float(u[i] << 16), __uint_as_float(u[i] & 0xffff0000u));
     } else {
-      __half2 h = *reinterpret_cast<const __half2*>(&u[i]);
-      const float2 t = __half22float2(h);
-      f[2 * i] = t.x;
-      f[2 * i + 1] = t.y;
+      f[i] = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
     }
   }
 }
 
-// Code for one value, returned in the low byte: clamp(rint(x*inv), -128, 127).
-// Adding 1.5*2^23 rounds to the nearest integer (ties to even) and leaves it in
-// the low mantissa bits; the lower clamp also maps NaN to -128 as fmaxf does in
-// the reference.  No upper clamp is needed: |x| <= absmax and
-// inv = 1/(sqrt(G)*scale) with scale >= absmax/(127*sqrt(G)) bound x*inv by
-// 127*(1+2^-22), which rounds to 127.
-__device__ __forceinline__ uint32_t code_bits(float x, float inv) {
-  float t = __fmul_rn(x, inv);
-  t = fmaxf(t, -128.0f);
-  return __float_as_uint(__fadd_rn(t, 12582912.0f));
+// Codes for two values, each returned in the low byte of its word:
+// clamp(rint(x*inv), -128, 127).  Adding 1.5*2^23 rounds to the nearest integer
+// (ties to even) and leaves it in the low mantissa bits; the lower clamp also
+// maps NaN to -128 as fmaxf does in the reference.  No upper clamp is needed:
+// |x| <= absmax and inv = 1/(sqrt(G)*scale) with scale >= absmax/(127*sqrt(G))
+// bound x*inv by 127*(1+2^-22), which rounds to 127.
+__device__ __forceinline__ uint2 code_bits2(float2 x, float2 inv2) {
+  float2 t = mul2(x, inv2);
+  t.x = fmaxf(t.x, -128.0f);
+  t.y = fmaxf(t.y, -128.0f);
+  t = add2(t, make_float2(12582912.0f, 12582912.0f));
+  return make_uint2(__float_as_uint(t.x), __float_as_uint(t.y));
 }
 
-__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+__device__ __forceinline__ uint32_t pack4(uint2 a, uint2 b) {
+  return __byte_perm(__byte_perm(a.x, a.y, 0x0040), __byte_perm(b.x, b.y, 0x0040), 0x5410);
 }
 
 template <int NST, bool BF16>
-__global__ void __launch_bounds__(512) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
+__global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
                                                        const RotQuantParams p) {
-  constexpr float kRoot = float(1 << NST);          // sqrt(G)
+  constexpr float kRoot = float(1 << NST);               // sqrt(G)
   constexpr float kQmaxRoot = 127.0f * float(1 << NST);  // 2032 for G = 256
 
   extern __shared__ uint8_t smem_raw[];
@@ -167,22 +221,22 @@ __global__ void __launch_bounds__(512) rotquant_kernel(const __grid_constant__ C
     uint8_t* buf = smem + size_t(s) * p.stage_bytes;
 
     // ---- own line (64 values) from the swizzled stage buffer ------------------
-    float v[64];
+    float2 vp[32];
     {
       const uint32_t line = uint32_t(tid);
       const uint8_t* lp = buf + line * 128u;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 w = *reinterpret_cast<const uint4*>(lp + ((uint32_t(c) ^ (line & 7u)) << 4));
-        unpack8<BF16>(w, &v[8 * c]);
+        unpack8<BF16>(w, &vp[4 * c]);
       }
     }
-    stage64<0>(v);
-    if (NST >= 2) stage64<1>(v);
-    if (NST >= 3) stage64<2>(v);
+    stage0_64(vp);
+    if (NST >= 2) stage1_64(vp);
+    if (NST >= 3) stage2_64(vp);
 
     float amax = 0.0f;
-    float w4[4][16];  // NST == 4 only: [input c][column j] of this thread's block
+    float2 w2[4][8];  // NST == 4 only: [input c][column pair] of this thread's block
     if (NST == 4) {
       // Swap 16-value blocks among the four threads of a group through this
       // warp's 4 KB slice of the stage buffer (its own lines, already read).
@@ -201,9 +255,9 @@ __global__ void __launch_bounds__(512) rotquant_kernel(const __grid_constant__ C
         for (int b = 0; b < 4; ++b) {
 #pragma unroll
           for (int jj = 0; jj < 2; ++jj) {
-            const int o = 16 * b + 8 * half + 4 * jj;
+            const int o = 8 * b + 4 * half + 2 * jj;  // pair index of value 16b + 8half + 4jj
             *reinterpret_cast<float4*>(xb + lane * 128 + ((uint32_t(2 * b + jj) ^ fw) << 4)) =
-                make_float4(v[o], v[o + 1], v[o + 2], v[o + 3]);
+                make_float4(vp[o].x, vp[o].y, vp[o + 1].x, vp[o + 1].y);
           }
         }
         __syncwarp();
@@ -214,11 +268,9 @@ __global__ void __launch_bounds__(512) rotquant_kernel(const __grid_constant__ C
           for (int jj = 0; jj < 2; ++jj) {
             const float4 t = *reinterpret_cast<const float4*>(xb + (4 * gq + c) * 128 +
                                                               ((uint32_t(2 * qd + jj) ^ fr) << 4));
-            const int j = 8 * half + 4 * jj;
-            w4[c][j] = t.x;
-            w4[c][j + 1] = t.y;
-            w4[c][j + 2] = t.z;
-            w4[c][j + 3] = t.w;
+            const int jp = 4 * half + 2 * jj;
+            w2[c][jp] = make_float2(t.x, t.y);
+            w2[c][jp + 1] = make_float2(t.z, t.w);
           }
         }
         __syncwarp();
@@ -226,16 +278,14 @@ __global__ void __launch_bounds__(512) rotquant_kernel(const __grid_constant__ C
       // The next TMA into this slot must not overtake these generic accesses.
       fence_proxy_async_smem();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        bfly4(w4[0][j], w4[1][j], w4[2][j], w4[3][j]);
-        amax = fmaxf(amax, fabsf(w4[0][j]));
-        amax = fmaxf(amax, fabsf(w4[1][j]));
-        amax = fmaxf(amax, fabsf(w4[2][j]));
-        amax = fmaxf(amax, fabsf(w4[3][j]));
+      for (int jp = 0; jp < 8; ++jp) {
+        bfly4x2(w2[0][jp], w2[1][jp], w2[2][jp], w2[3][jp]);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) amax = absmax3(amax, w2[r][jp].x, w2[r][jp].y);
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      for (int i = 0; i < 32; ++i) amax = absmax3(amax, vp[i].x, vp[i].y);
     }
 
     // ---- row absmax -----------------------------------------------------------
@@ -260,6 +310,7 @@ __global__ void __launch_bounds__(512) rotquant_kernel(const __grid_constant__ C
       const float sc = fmaxf(__fdiv_rn(am, kQmaxRoot), 1e-30f);
       if (chunk == 0) p.scale[row] = sc;
       const float inv = __fdiv_rn(1.0f, __fmul_rn(sc, kRoot));
+      const float2 inv2 = make_float2(inv, inv);
       if (NST == 4) {
         int8_t* qp = p.q + row * int64_t(p.K) + (chunk >> 2) * 256 + (chunk & 3) * 16;
 #pragma unroll
@@ -267,8 +318,7 @@ __global__ void __launch_bounds__(512) rotquant_kernel(const __grid_constant__ C
           uint32_t wd[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            wd[k] = pack4(code_bits(w4[r][4 * k], inv), code_bits(w4[r][4 * k + 1], inv),
-                          code_bits(w4[r][4 * k + 2], inv), code_bits(w4[r][4 * k + 3], inv));
+            wd[k] = pack4(code_bits2(w2[r][2 * k], inv2), code_bits2(w2[r][2 * k + 1], inv2));
           *reinterpret_cast<uint4*>(qp + r * 64) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
         }
       } else {
@@ -278,9 +328,8 @@ __global__ void __launch_bounds__(512) rotquant_kernel(const __grid_constant__ C
           uint32_t wd[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const int i = 16 * c + 4 * k;
-            wd[k] = pack4(code_bits(v[i], inv), code_bits(v[i + 1], inv), code_bits(v[i + 2], inv),
-                          code_bits(v[i + 3], inv));
+            const int i = 8 * c + 2 * k;  // pair index of value 16c + 4k
+            wd[k] = pack4(code_bits2(vp[i], inv2), code_bits2(vp[i + 1], inv2));
           }
           *reinterpret_cast<uint4*>(qp + c * 16) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
         }

@@ -85,19 +85,21 @@ int tg_int8_gemm_dequant(const int8_t *xq, const float *xscale, const int8_t *wq
                          int64_t K, int out_dtype, void *out, void *stream);
 
 /*
- * Tile width (UMMA N: 256, 224, 192, 160 or 128) tg_int8_gemm_dequant will use
- * for an M x N problem on the current device, or -1 if no device is usable.
- * The width minimises (persistent waves) x (tile cost) over the SMs.  No
- * reference counterpart (cuBLASLt picked its own tiles).
+ * The tile shape tg_int8_gemm_dequant uses for an M x N problem on the
+ * current device: *bn = tile width (UMMA N: 256, 224, 192, 160 or 128) and
+ * *pair = 1 when the tile is 256 rows computed by a pair of SMs (tcgen05
+ * cta_group::2), 0 for 128-row single-SM tiles.  The width minimises
+ * (persistent waves) x (tile cost).  No reference counterpart (cuBLASLt chose
+ * its own tiles).
  */
-int tg_gemm_tile_width(int64_t M, int64_t N);
+int tg_gemm_config(int64_t M, int64_t N, int *bn, int *pair);
 
 /*
- * Force the GEMM tile width for every later call in this process (0 restores
- * the automatic choice).  For tests and tuning; returns TG_ERR_INVALID_ARG for
- * a width the library was not built with.
+ * Force the GEMM tile shape for every later call in this process: bn 0 or one
+ * of the widths above, pair -1 (automatic), 0 or 1.  For tests and tuning;
+ * TG_ERR_INVALID_ARG for anything else.
  */
-int tg_set_gemm_tile_width(int bn);
+int tg_set_gemm_config(int bn, int pair);
 
 /*
  * Read (and optionally clear) the device status word of `device`, which

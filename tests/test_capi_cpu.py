@@ -48,8 +48,9 @@ def test_argument_checks_return_before_device_work():
     assert L.tg_int8_gemm_dequant(p, p, p, p, 3, None, 0, 4, 64, 32, 1, p, None) == _lib.TG_ERR_INVALID_ARG
     assert L.tg_int8_gemm_dequant(p, p, p, p, 1, None, 0, 4, 64, 32, 7, p, None) == _lib.TG_ERR_INVALID_ARG
     assert L.tg_int8_gemm_dequant(None, None, None, None, 1, None, 0, 0, 64, 32, 1, None, None) == _lib.TG_OK
-    assert L.tg_set_gemm_tile_width(100) == _lib.TG_ERR_INVALID_ARG
-    assert L.tg_set_gemm_tile_width(0) == _lib.TG_OK
+    assert L.tg_set_gemm_config(100, -1) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_set_gemm_config(256, 2) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_set_gemm_config(0, -1) == _lib.TG_OK
 
 
 def test_check_maps_status_to_exceptions():

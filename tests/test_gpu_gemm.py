@@ -107,21 +107,24 @@ def test_full_size_bit_exact_vs_torch_sequence(cuda, shape):
         assert torch.equal(y.view(torch.int16), ref.view(torch.int16)), (shape, out_dtype)
 
 
+@pytest.mark.parametrize("pair", [0, 1])
 @pytest.mark.parametrize("bn", [256, 224, 192, 160, 128])
-def test_every_tile_width_bit_exact(cuda, bn):
-    L = _lib.lib()
-    assert L.tg_set_gemm_tile_width(bn) == 0
+def test_every_tile_shape_bit_exact(cuda, bn, pair):
+    _lib.set_gemm_config(bn, pair)
     try:
         for out_dtype in DTS:
             _check_vs_oracle(_rand_case(300, 600, 1024, seed=bn, bias_dtype=torch.bfloat16), out_dtype, cuda)
+        _check_vs_oracle(_rand_case(1, 72, 256, seed=3), torch.float16, cuda)        # one row
+        _check_vs_oracle(_rand_case(513, 264, 5120, seed=4), torch.bfloat16, cuda)   # ragged M and N
     finally:
-        L.tg_set_gemm_tile_width(0)
+        _lib.set_gemm_config(0, -1)
 
 
-def test_tile_width_choice_for_dit_shapes(cuda):
-    L = _lib.lib()
-    widths = {n: L.tg_gemm_tile_width(4096, n) for n in (15360, 5120, 13824)}
-    assert widths[15360] == 256 and widths[13824] == 256 and widths[5120] == 224
+def test_tile_shape_choice_for_dit_shapes(cuda):
+    for n in (15360, 5120, 13824):
+        bn, pair = _lib.gemm_config(4096, n)
+        assert pair == 1 and bn in (256, 224, 192, 160, 128)
+    assert _lib.gemm_config(64, 5120)[1] == 0
 
 
 def test_empty_and_rejected(cuda):

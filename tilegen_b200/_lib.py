@@ -99,10 +99,10 @@ def lib() -> ctypes.CDLL:
         L.tg_rotate_quant_max_k.restype = i64
         L.tg_int8_gemm_dequant.argtypes = [p, p, p, p, i64, p, i32, i64, i64, i64, i32, p, p]
         L.tg_int8_gemm_dequant.restype = i32
-        L.tg_gemm_tile_width.argtypes = [i64, i64]
-        L.tg_gemm_tile_width.restype = i32
-        L.tg_set_gemm_tile_width.argtypes = [i32]
-        L.tg_set_gemm_tile_width.restype = i32
+        L.tg_gemm_config.argtypes = [i64, i64, ctypes.POINTER(i32), ctypes.POINTER(i32)]
+        L.tg_gemm_config.restype = i32
+        L.tg_set_gemm_config.argtypes = [i32, i32]
+        L.tg_set_gemm_config.restype = i32
         L.tg_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint32), i32]
         L.tg_device_status.restype = i32
         _lib = L
@@ -115,6 +115,18 @@ def check(func: str, status: int) -> None:
         if status in (TG_ERR_INVALID_ARG, TG_ERR_UNSUPPORTED, TG_ERR_MISALIGNED):
             raise ValueError(f"{func}: {msg} (status {status})")
         raise TileGenError(func, status, msg)
+
+
+def gemm_config(m: int, n: int) -> tuple[int, int]:
+    """(tile width, pair flag) the GEMM uses for an m x n problem on the current device."""
+    bn, pair = ctypes.c_int(0), ctypes.c_int(0)
+    check("tg_gemm_config", lib().tg_gemm_config(int(m), int(n), ctypes.byref(bn), ctypes.byref(pair)))
+    return bn.value, pair.value
+
+
+def set_gemm_config(bn: int = 0, pair: int = -1) -> None:
+    """Force the GEMM tile shape (bn 0 / pair -1 restore the automatic choice)."""
+    check("tg_set_gemm_config", lib().tg_set_gemm_config(int(bn), int(pair)))
 
 
 def device_status(device: int, clear: bool = True) -> int:

@@ -213,55 +213,111 @@ int tg_rotate_quant(const void* x, int x_dtype, int64_t M, int64_t K, int group,
 
 namespace {
 
-template <int BN, int OUT, bool HAS_BIAS>
+template <int BN, int OUT, bool HAS_BIAS, bool PAIR>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const tg::GemmParams& p,
-                  int dev, int sms, cudaStream_t st) {
+                  int dev, int units, cudaStream_t st) {
   static uint32_t attr_done[kMaxDevices];
-  constexpr uint32_t smem = tg::gemm::smem_bytes<BN>();
-  auto kern = tg::gemm_i8_dequant_kernel<BN, OUT, HAS_BIAS>;
+  constexpr uint32_t smem = tg::gemm::smem_bytes(BN, PAIR);
+  auto kern = tg::gemm_i8_dequant_kernel<BN, OUT, HAS_BIAS, PAIR>;
   if (!ensure_smem_attr(kern, dev, smem, attr_done)) return TG_ERR_CUDA;
   const int tiles = p.m_tiles * p.n_tiles;
-  const int grid = tiles < sms ? tiles : sms;
-  kern<<<dim3(unsigned(grid)), dim3(tg::gemm::THREADS), smem, st>>>(ta, tb, to, p);
+  const int grid_units = tiles < units ? tiles : units;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(unsigned(grid_units * (PAIR ? 2 : 1)));
+  cfg.blockDim = dim3(tg::gemm::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = PAIR ? 2 : 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, to, p) != cudaSuccess) return TG_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const tg::GemmParams& p,
-                   int out_dtype, bool has_bias, int dev, int sms, cudaStream_t st) {
+                   int out_dtype, bool has_bias, int dev, int units, cudaStream_t st) {
   switch (out_dtype) {
-    case TG_DT_F32: return has_bias ? launch_gemm_t<BN, 0, true>(ta, tb, to, p, dev, sms, st)
-                                    : launch_gemm_t<BN, 0, false>(ta, tb, to, p, dev, sms, st);
-    case TG_DT_F16: return has_bias ? launch_gemm_t<BN, 1, true>(ta, tb, to, p, dev, sms, st)
-                                    : launch_gemm_t<BN, 1, false>(ta, tb, to, p, dev, sms, st);
-    default: return has_bias ? launch_gemm_t<BN, 2, true>(ta, tb, to, p, dev, sms, st)
-                             : launch_gemm_t<BN, 2, false>(ta, tb, to, p, dev, sms, st);
+    case TG_DT_F32: return has_bias ? launch_gemm_t<BN, 0, true, PAIR>(ta, tb, to, p, dev, units, st)
+                                    : launch_gemm_t<BN, 0, false, PAIR>(ta, tb, to, p, dev, units, st);
+    case TG_DT_F16: return has_bias ? launch_gemm_t<BN, 1, true, PAIR>(ta, tb, to, p, dev, units, st)
+                                    : launch_gemm_t<BN, 1, false, PAIR>(ta, tb, to, p, dev, units, st);
+    default: return has_bias ? launch_gemm_t<BN, 2, true, PAIR>(ta, tb, to, p, dev, units, st)
+                             : launch_gemm_t<BN, 2, false, PAIR>(ta, tb, to, p, dev, units, st);
   }
 }
 
-// Tile width for an M x N problem on `sms` SMs: the persistent grid runs
-// ceil(tiles / sms) waves of tiles costing about (BN + kTileOverhead) column
-// steps each, so pick the width that minimises waves * (BN + overhead).
+template <bool PAIR>
+int launch_gemm_mode(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                     const tg::GemmParams& p, int out_dtype, bool hb, int dev, int units, cudaStream_t st) {
+  switch (bn) {
+    case 224: return launch_gemm_bn<224, PAIR>(ta, tb, to, p, out_dtype, hb, dev, units, st);
+    case 192: return launch_gemm_bn<192, PAIR>(ta, tb, to, p, out_dtype, hb, dev, units, st);
+    case 160: return launch_gemm_bn<160, PAIR>(ta, tb, to, p, out_dtype, hb, dev, units, st);
+    case 128: return launch_gemm_bn<128, PAIR>(ta, tb, to, p, out_dtype, hb, dev, units, st);
+    default: return launch_gemm_bn<256, PAIR>(ta, tb, to, p, out_dtype, hb, dev, units, st);
+  }
+}
+
+// Tile-processing units that can be resident at once: SMs for single-CTA
+// tiles, co-resident clusters of 2 for pair tiles (queried once per device).
+int gemm_units(int dev, int sms, bool pair) {
+  static int cache[kMaxDevices];
+  if (!pair) return sms;
+  if (cache[dev] > 0) return cache[dev];
+  auto kern = tg::gemm_i8_dequant_kernel<256, 1, false, true>;
+  constexpr uint32_t smem = tg::gemm::smem_bytes(256, true);
+  static uint32_t attr_done[kMaxDevices];
+  int n = 0;
+  if (ensure_smem_attr(kern, dev, smem, attr_done)) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(unsigned(sms));
+    cfg.blockDim = dim3(tg::gemm::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  }
+  cache[dev] = n > 0 ? n : sms / 2;
+  return cache[dev];
+}
+
+// Tile shape for an M x N problem.  The persistent grid runs
+// ceil(tiles / units) waves of tiles costing about (BN + kTileOverhead) column
+// steps each; pick the width minimising waves * (BN + overhead).  Pair tiles
+// (256 rows on two SMs) are used whenever M has more than one 128-row block.
 constexpr int kGemmWidths[] = {256, 224, 192, 160, 128};
 constexpr int kTileOverhead = 32;
+int g_forced_bn = 0;     // tg_set_gemm_config(): 0 = cost model
+int g_forced_pair = -1;  // -1 = by M
 
-int g_forced_bn = 0;  // tg_set_gemm_tile_width(); 0 = pick by the cost model
-
-int pick_gemm_bn(int64_t M, int64_t N, int sms) {
-  if (g_forced_bn) return g_forced_bn;
-  const int64_t mt = (M + tg::gemm::BM - 1) / tg::gemm::BM;
+void pick_gemm_config(int64_t M, int64_t N, int dev, int sms, int* bn_out, int* pair_out) {
+  const bool pair = g_forced_pair >= 0 ? g_forced_pair != 0 : M > tg::gemm::BM;
+  const int units = gemm_units(dev, sms, pair);
+  const int64_t tm = pair ? 2 * tg::gemm::BM : tg::gemm::BM;
+  const int64_t mt = (M + tm - 1) / tm;
   int best = 256;
   int64_t best_cost = -1;
   for (int bn : kGemmWidths) {
     const int64_t tiles = mt * ((N + bn - 1) / bn);
-    const int64_t waves = (tiles + sms - 1) / sms;
+    const int64_t waves = (tiles + units - 1) / units;
     const int64_t cost = waves * (bn + kTileOverhead);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = bn;
     }
   }
-  return best;
+  *bn_out = g_forced_bn ? g_forced_bn : best;
+  *pair_out = pair ? 1 : 0;
 }
 
 }  // namespace
@@ -290,7 +346,8 @@ int tg_int8_gemm_dequant(const int8_t* xq, const float* xscale, const int8_t* wq
   DeviceInfo info;
   if (!current_device(&dev, &info)) return TG_ERR_CUDA;
 
-  const int bn = pick_gemm_bn(M, N, info.sms);
+  int bn, pair;
+  pick_gemm_config(M, N, dev, info.sms, &bn, &pair);
   const int ch_bytes = (bn * esz) % 128 == 0 ? 128 : 64;  // epilogue chunk row bytes (kernel's CH_BYTES)
 
   CUtensorMap ta, tb, to;
@@ -298,7 +355,7 @@ int tg_int8_gemm_dequant(const int8_t* xq, const float* xscale, const int8_t* wq
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return TG_ERR_CUDA;
   if (!make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, uint64_t(K), uint64_t(N), uint64_t(K), BK,
-                    uint32_t(bn), CU_TENSOR_MAP_SWIZZLE_128B))
+                    uint32_t(tg::gemm::b_rows(bn, pair != 0)), CU_TENSOR_MAP_SWIZZLE_128B))
     return TG_ERR_CUDA;
   const CUtensorMapDataType odt = out_dtype == TG_DT_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                   : out_dtype == TG_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -316,39 +373,34 @@ int tg_int8_gemm_dequant(const int8_t* xq, const float* xscale, const int8_t* wq
   p.M = int(M);
   p.N = int(N);
   p.K = int(K);
-  p.m_tiles = int((M + BM - 1) / BM);
+  p.m_tiles = int((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
   p.n_tiles = int((N + bn - 1) / bn);
   p.k_blocks = int((K + BK - 1) / BK);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool hb = bias != nullptr;
-  switch (bn) {
-    case 224: return launch_gemm_bn<224>(ta, tb, to, p, out_dtype, hb, dev, info.sms, st);
-    case 192: return launch_gemm_bn<192>(ta, tb, to, p, out_dtype, hb, dev, info.sms, st);
-    case 160: return launch_gemm_bn<160>(ta, tb, to, p, out_dtype, hb, dev, info.sms, st);
-    case 128: return launch_gemm_bn<128>(ta, tb, to, p, out_dtype, hb, dev, info.sms, st);
-    default: return launch_gemm_bn<256>(ta, tb, to, p, out_dtype, hb, dev, info.sms, st);
-  }
+  const int units = gemm_units(dev, info.sms, pair != 0);
+  return pair ? launch_gemm_mode<true>(bn, ta, tb, to, p, out_dtype, hb, dev, units, st)
+              : launch_gemm_mode<false>(bn, ta, tb, to, p, out_dtype, hb, dev, units, st);
 }
 
-int tg_set_gemm_tile_width(int bn) {
-  if (bn == 0) {
-    g_forced_bn = 0;
-    return TG_OK;
-  }
-  for (int w : kGemmWidths)
-    if (w == bn) {
-      g_forced_bn = bn;
-      return TG_OK;
-    }
-  return TG_ERR_INVALID_ARG;
+int tg_set_gemm_config(int bn, int pair) {
+  if (pair < -1 || pair > 1) return TG_ERR_INVALID_ARG;
+  bool ok = bn == 0;
+  for (int w : kGemmWidths) ok = ok || w == bn;
+  if (!ok) return TG_ERR_INVALID_ARG;
+  g_forced_bn = bn;
+  g_forced_pair = pair;
+  return TG_OK;
 }
 
-int tg_gemm_tile_width(int64_t M, int64_t N) {
+int tg_gemm_config(int64_t M, int64_t N, int* bn, int* pair) {
+  if (!bn || !pair) return TG_ERR_INVALID_ARG;
   int dev;
   DeviceInfo info;
-  if (!current_device(&dev, &info)) return -1;
-  return pick_gemm_bn(M, N, info.sms);
+  if (!current_device(&dev, &info)) return TG_ERR_CUDA;
+  pick_gemm_config(M, N, dev, info.sms, bn, pair);
+  return TG_OK;
 }
 
 int tg_device_status(int device, uint32_t* bits, int clear) {

@@ -7,19 +7,28 @@
 // int32/fp32 temporaries: the int32 accumulators live in tensor memory and the
 // fp32 epilogue runs on them in registers.
 //
-// Structure (one persistent CTA per SM, 192 threads):
-//   warp 0      TMA producer: A tile [128 x 128 B] and B tile [256 x 128 B] per
-//               k-block into a 4-deep shared-memory ring (128-byte swizzle).
-//   warp 1      allocates 512 TMEM columns; one lane issues tcgen05.mma
-//               kind::i8 (M=128, N=256, K=32; four per k-block) into one of two
-//               256-column int32 accumulators, and commits each ring slot back
-//               to the producer and each finished accumulator to the epilogue.
-//   warps 2-5   epilogue: tcgen05.ld 32 rows x 64 columns at a time, int32 ->
-//               fp32 (round to nearest), * xscale, * wscale, + bias, convert, and
-//               a swizzled shared-memory tile stored with a TMA bulk tensor store.
-// Tiles are walked M-fastest so the CTAs in flight share the same weight
-// columns in L2.  Two accumulators let the epilogue of tile i overlap the MMAs
-// of tile i+1.  Every mbarrier wait is bounded (see common.cuh).
+// Structure (persistent, one CTA per SM, 192 threads):
+//   warp 0      TMA producer: A tile [128 x 128 B] and B tile [BN(/2) x 128 B]
+//               per k-block into a shared-memory ring (128-byte swizzle).
+//   warp 1      allocates 512 TMEM columns; one lane issues tcgen05.mma kind::i8
+//               (K=32 per instruction, four per k-block) into one of two int32
+//               accumulators (TMEM columns 0 and 256), and commits each ring
+//               slot back to the producer and each finished accumulator to the
+//               epilogue.
+//   warps 2-5   epilogue: tcgen05.ld 32 rows x one chunk of columns, int32 ->
+//               fp32 (round to nearest), * xscale, * wscale, + bias, convert,
+//               then a swizzled shared-memory chunk stored by a TMA bulk tensor
+//               store.
+// PAIR = false: each CTA computes a 128 x BN tile (cta_group::1, M=128).
+// PAIR = true: the two CTAs of a cluster compute one 256 x BN tile with the
+//   pair MMA (cta_group::2, M=256): each CTA loads its 128 rows of A and half
+//   (BN/2 rows) of B, so per SM the operand traffic per MMA is a third lower.
+//   Both CTAs' loads complete on the even CTA's ring barriers; its MMA thread
+//   issues for the pair and its commits arrive on both CTAs' barriers; both
+//   epilogues release an accumulator by arriving on the even CTA's barrier.
+// Tiles are walked M-fastest so the CTAs in flight share weight columns in L2.
+// Every mbarrier wait is bounded (see common.cuh); a role that gives up stops
+// the others in its CTA, and the peer CTA's waits then expire as well.
 #pragma once
 
 #include "common.cuh"
@@ -27,26 +36,34 @@
 namespace tg {
 
 namespace gemm {
-constexpr int BM = 128;               // rows of xq per tile (UMMA M)
+constexpr int BM = 128;               // rows of xq per CTA (UMMA M per CTA)
 constexpr int BN_MAX = 256;           // widest tile (rows of wq per tile, UMMA N)
 constexpr int BK = 128;               // bytes (= int8 elements) of K per k-block
 constexpr int UK = 32;                // K per tcgen05.mma kind::i8
-constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK;      // 16 KB
 constexpr int OUT_BYTES = 32 * 128;   // one 32-row x 128-byte epilogue chunk per warp
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;        // two accumulators, at columns 0 and 256
+constexpr uint32_t SMEM_LIMIT = 232448;
 
-template <int BN>
-__host__ __device__ constexpr uint32_t smem_bytes() {
-  return STAGES * (A_BYTES + BN * BK) + 4 * OUT_BYTES + 1024;
+// Rows of B each CTA holds, bytes of one ring slot, ring depth, dynamic smem.
+__host__ __device__ constexpr int b_rows(int bn, bool pair) { return pair ? bn / 2 : bn; }
+__host__ __device__ constexpr uint32_t stage_bytes(int bn, bool pair) {
+  return uint32_t(A_BYTES + b_rows(bn, pair) * BK);
+}
+__host__ __device__ constexpr int stages(int bn, bool pair) {
+  return int((SMEM_LIMIT - 4 * OUT_BYTES - 1024 - 4096) / stage_bytes(bn, pair)) > 8
+             ? 8
+             : int((SMEM_LIMIT - 4 * OUT_BYTES - 1024 - 4096) / stage_bytes(bn, pair));
+}
+__host__ __device__ constexpr uint32_t smem_bytes(int bn, bool pair) {
+  return uint32_t(stages(bn, pair)) * stage_bytes(bn, pair) + 4 * OUT_BYTES + 1024;
 }
 
 // tcgen05 instruction descriptor: D=S32 (bits 4-5 = 2), A=B=S8 (bits 7-9 and
 // 10-12 = 1), both K-major, N>>3 at bits 17-22, M>>4 at bits 24-28.
-template <int BN>
-__host__ __device__ constexpr uint32_t idesc() {
-  return (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
 // Shared-memory matrix descriptor for a K-major operand tile stored as rows
@@ -66,12 +83,12 @@ struct GemmParams {
   int bias_dtype;  // tg_dtype
   int wscale_bcast;
   int M, N, K;
-  int m_tiles, n_tiles, k_blocks;
+  int m_tiles, n_tiles, k_blocks;  // m_tiles counts 128-row (single) or 256-row (pair) tiles
 };
 
 // BN: tile width (a multiple of 32, at most 256); OUT: 0 fp32, 1 fp16, 2 bf16
-// (tg_dtype codes).
-template <int BN, int OUT, bool HAS_BIAS>
+// (tg_dtype codes); PAIR: see above (launched with clusters of 2 CTAs).
+template <int BN, int OUT, bool HAS_BIAS, bool PAIR>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_i8_dequant_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                            const __grid_constant__ CUtensorMap tma_out, const GemmParams p) {
@@ -83,18 +100,22 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   constexpr int CH_BYTES = (BN * ESZ) % 128 == 0 ? 128 : 64;
   constexpr int CH = CH_BYTES / ESZ;   // output columns per epilogue chunk
   constexpr int NCH = BN / CH;         // chunks per tile
-  constexpr int B_BYTES = BN * BK;
-  constexpr uint32_t IDESC = idesc<BN>();
+  constexpr int S = stages(BN, PAIR);
+  constexpr int BROWS = b_rows(BN, PAIR);
+  constexpr uint32_t B_BYTES = uint32_t(BROWS) * BK;
+  constexpr int TILE_M = PAIR ? 2 * BM : BM;
+  constexpr uint32_t IDESC = idesc(TILE_M, BN);
+  constexpr uint32_t TX_BYTES = (PAIR ? 2u : 1u) * (uint32_t(A_BYTES) + B_BYTES);
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sOut = sB + STAGES * B_BYTES;
+  uint8_t* sB = smem + S * A_BYTES;
+  uint8_t* sOut = sB + S * B_BYTES;
 
-  __shared__ __align__(8) uint64_t full_bar[STAGES];
-  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t full_bar[S];
+  __shared__ __align__(8) uint64_t empty_bar[S];
   __shared__ __align__(8) uint64_t tfull_bar[2];
   __shared__ __align__(8) uint64_t tempty_bar[2];
   __shared__ uint32_t tmem_base_sh;
@@ -104,29 +125,38 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);   // tile-processing unit
+  const int units = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
   const int num_tiles = p.m_tiles * p.n_tiles;
 
   if (threadIdx.x == 0) {
     prefetch_tmap(&tma_a);
     prefetch_tmap(&tma_b);
     prefetch_tmap(&tma_out);
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 4);
+      mbar_init(&tempty_bar[b], PAIR ? 8 : 4);
     }
     fence_mbar_init();
     abort_flag = 0;
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_base_sh, TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(&tmem_base_sh, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&tmem_base_sh, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
 
@@ -151,15 +181,24 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-        const int m0 = (t % p.m_tiles) * BM;
-        const int n0 = (t / p.m_tiles) * BN;
+      for (int t = unit; t < num_tiles; t += units) {
+        const int m0 = (t % p.m_tiles) * TILE_M + int(rank) * BM;
+        const int n0 = (t / p.m_tiles) * BN + int(rank) * BROWS;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!wait(&empty_bar[stage], phase ^ 1u, DEVERR_PIPE_TIMEOUT)) goto done;
-          mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
-          tma_load_2d(sA + stage * A_BYTES, &tma_a, &full_bar[stage], kb * BK, m0);
-          tma_load_2d(sB + stage * B_BYTES, &tma_b, &full_bar[stage], kb * BK, n0);
-          if (++stage == STAGES) {
+          if (PAIR) {
+            // Both CTAs' copies land on the even CTA's barrier, which expects
+            // the bytes of both.
+            const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], TX_BYTES);
+            tma_load_2d_pair(sA + stage * A_BYTES, &tma_a, fb, kb * BK, m0);
+            tma_load_2d_pair(sB + stage * B_BYTES, &tma_b, fb, kb * BK, n0);
+          } else {
+            mbar_arrive_expect_tx(&full_bar[stage], TX_BYTES);
+            tma_load_2d(sA + stage * A_BYTES, &tma_a, &full_bar[stage], kb * BK, m0);
+            tma_load_2d(sB + stage * B_BYTES, &tma_b, &full_bar[stage], kb * BK, n0);
+          }
+          if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
@@ -168,11 +207,11 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      for (int t = unit; t < num_tiles; t += units, ++local) {
         const int ab = local & 1;
         const uint32_t acc_phase = uint32_t(local >> 1) & 1u;
         if (!wait(&tempty_bar[ab], acc_phase ^ 1u, DEVERR_PIPE_TIMEOUT)) goto done;
@@ -185,16 +224,21 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / UK; ++k) {
-            mma_i8(d_tmem, kmajor_sw128_desc(a_addr + k * UK), kmajor_sw128_desc(b_addr + k * UK), IDESC,
-                   (kb | k) != 0 ? 1u : 0u);
+            const uint64_t ad = kmajor_sw128_desc(a_addr + k * UK);
+            const uint64_t bd = kmajor_sw128_desc(b_addr + k * UK);
+            const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+            if (PAIR) mma_i8_pair(d_tmem, ad, bd, IDESC, acc);
+            else mma_i8(d_tmem, ad, bd, IDESC, acc);
           }
-          mma_commit(&empty_bar[stage]);  // slot is free once these MMAs have read it
-          if (++stage == STAGES) {
+          // The slot is free once these MMAs have read it (in both CTAs).
+          if (PAIR) mma_commit_pair(&empty_bar[stage], 0x3); else mma_commit(&empty_bar[stage]);
+          if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        mma_commit(&tfull_bar[ab]);  // accumulator complete
+        // Accumulator complete (both CTAs' halves).
+        if (PAIR) mma_commit_pair(&tfull_bar[ab], 0x3); else mma_commit(&tfull_bar[ab]);
       }
     }
   } else {
@@ -202,9 +246,11 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     const int et = threadIdx.x - 64;      // 0..127
     const int quarter = warp & 3;         // TMEM lanes [32*quarter, +32)
     uint8_t* sbuf = sOut + (warp - 2) * OUT_BYTES;
+    const uint32_t tempty_leader0 = PAIR ? mapa_shared(smem_u32(&tempty_bar[0]), 0) : 0u;
+    const uint32_t tempty_leader1 = PAIR ? mapa_shared(smem_u32(&tempty_bar[1]), 0) : 0u;
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
-      const int m0 = (t % p.m_tiles) * BM;
+    for (int t = unit; t < num_tiles; t += units, ++local) {
+      const int m0 = (t % p.m_tiles) * TILE_M + int(rank) * BM;
       const int n0 = (t / p.m_tiles) * BN;
       const int ab = local & 1;
       // Column parameters of this tile (shared by the four epilogue warps).
@@ -243,7 +289,10 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           // This warp is done reading the accumulator: hand it back to the MMA.
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty_bar[ab]);
+          if (lane == 0) {
+            if (PAIR) mbar_arrive_cluster(ab ? tempty_leader1 : tempty_leader0);
+            else mbar_arrive(&tempty_bar[ab]);
+          }
         }
         // The previous chunk's TMA store must have finished reading sbuf.
         if (lane == 0) bulk_wait_read<0>();
@@ -255,7 +304,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 #pragma unroll
         for (int c16 = 0; c16 < CH_BYTES / 16; ++c16) {  // 16 output bytes per step
           uint32_t pk[4];
-          constexpr int PER = 16 / ESZ;       // values per 16 bytes
+          constexpr int PER = 16 / ESZ;                  // values per 16 bytes
 #pragma unroll
           for (int e = 0; e < PER; e += 4) {
             const int j = c16 * PER + e;
@@ -308,10 +357,13 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 done:
   __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  // Neither CTA of a pair may leave while the other can still touch its
+  // shared memory or tensor memory.
+  if (PAIR) cluster_sync(); else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 

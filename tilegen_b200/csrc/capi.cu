@@ -13,7 +13,7 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr int64_t kRotQuantMaxK = 32768;
-constexpr int kRotQuantRegs = 96;  // __maxnreg__ of rotquant_kernel
+constexpr int kRotQuantRegs = 104;  // __maxnreg__ of rotquant_kernel
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -163,7 +163,7 @@ int tg_rotate_quant(const void* x, int x_dtype, int64_t M, int64_t K, int group,
   }
   const uint32_t stage_bytes = uint32_t(threads) * 128u;
   // Ring depth: as deep as possible (up to 4) while the CTAs that the register
-  // budget allows per SM (96 registers a thread) still fit in shared memory.
+  // budget allows per SM (104 registers a thread) still fit in shared memory.
   int ctas = 65536 / (threads * kRotQuantRegs);
   ctas = ctas < 1 ? 1 : ctas;
   const uint32_t per_cta = 232448u / uint32_t(ctas) - 2048u - 1024u - uint32_t(3 * R) * 4u;
@@ -375,7 +375,7 @@ int tg_int8_gemm_dequant(const int8_t* xq, const float* xscale, const int8_t* wq
   p.K = int(K);
   p.m_tiles = int((M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
   p.n_tiles = int((N + bn - 1) / bn);
-  p.k_blocks = int((K + BK - 1) / BK);
+  p.k_blocks = int((K + int64_t(BK) * tg::gemm::ksub(pair != 0) - 1) / (int64_t(BK) * tg::gemm::ksub(pair != 0)));
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool hb = bias != nullptr;

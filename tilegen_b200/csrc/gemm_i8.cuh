@@ -46,10 +46,14 @@ constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;        // two accumulators, at columns 0 and 256
 constexpr uint32_t SMEM_LIMIT = 232448;
 
-// Rows of B each CTA holds, bytes of one ring slot, ring depth, dynamic smem.
+// Rows of B each CTA holds; 128-byte K sub-blocks per ring slot (pair tiles
+// take two, so the MMA thread waits once per 8 MMAs: a barrier wait costs the
+// issuing thread a few hundred cycles, more than 4 MMAs of a 128-row tile
+// take); bytes of one slot; ring depth; dynamic shared memory.
 __host__ __device__ constexpr int b_rows(int bn, bool pair) { return pair ? bn / 2 : bn; }
+__host__ __device__ constexpr int ksub(bool pair) { return pair ? 2 : 1; }
 __host__ __device__ constexpr uint32_t stage_bytes(int bn, bool pair) {
-  return uint32_t(A_BYTES + b_rows(bn, pair) * BK);
+  return uint32_t(ksub(pair) * (A_BYTES + b_rows(bn, pair) * BK));
 }
 __host__ __device__ constexpr int stages(int bn, bool pair) {
   return int((SMEM_LIMIT - 4 * OUT_BYTES - 1024 - 4096) / stage_bytes(bn, pair)) > 8
@@ -83,7 +87,8 @@ struct GemmParams {
   int bias_dtype;  // tg_dtype
   int wscale_bcast;
   int M, N, K;
-  int m_tiles, n_tiles, k_blocks;  // m_tiles counts 128-row (single) or 256-row (pair) tiles
+  int m_tiles, n_tiles, k_blocks;  // m_tiles: 128-row (single) or 256-row (pair) tiles;
+                                   // k_blocks: ring slots of ksub(pair) * 128 bytes of K
 };
 
 // BN: tile width (a multiple of 32, at most 256); OUT: 0 fp32, 1 fp16, 2 bf16
@@ -102,17 +107,20 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   constexpr int NCH = BN / CH;         // chunks per tile
   constexpr int S = stages(BN, PAIR);
   constexpr int BROWS = b_rows(BN, PAIR);
-  constexpr uint32_t B_BYTES = uint32_t(BROWS) * BK;
+  constexpr int KS = ksub(PAIR);
+  constexpr uint32_t B_BYTES = uint32_t(BROWS) * BK;       // one 128-byte K sub-block of B
+  constexpr uint32_t A_SLOT = uint32_t(KS) * A_BYTES;       // ring slot of A
+  constexpr uint32_t B_SLOT = uint32_t(KS) * B_BYTES;       // ring slot of B
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
   constexpr uint32_t IDESC = idesc(TILE_M, BN);
-  constexpr uint32_t TX_BYTES = (PAIR ? 2u : 1u) * (uint32_t(A_BYTES) + B_BYTES);
+  constexpr uint32_t TX_BYTES = (PAIR ? 2u : 1u) * (A_SLOT + B_SLOT);
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + S * A_BYTES;
-  uint8_t* sOut = sB + S * B_BYTES;
+  uint8_t* sB = smem + S * A_SLOT;
+  uint8_t* sOut = sB + S * B_SLOT;
 
   __shared__ __align__(8) uint64_t full_bar[S];
   __shared__ __align__(8) uint64_t empty_bar[S];
@@ -191,12 +199,20 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
             // the bytes of both.
             const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], TX_BYTES);
-            tma_load_2d_pair(sA + stage * A_BYTES, &tma_a, fb, kb * BK, m0);
-            tma_load_2d_pair(sB + stage * B_BYTES, &tma_b, fb, kb * BK, n0);
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+              const int kx = (kb * KS + ks) * BK;
+              tma_load_2d_pair(sA + stage * A_SLOT + ks * A_BYTES, &tma_a, fb, kx, m0);
+              tma_load_2d_pair(sB + stage * B_SLOT + ks * B_BYTES, &tma_b, fb, kx, n0);
+            }
           } else {
             mbar_arrive_expect_tx(&full_bar[stage], TX_BYTES);
-            tma_load_2d(sA + stage * A_BYTES, &tma_a, &full_bar[stage], kb * BK, m0);
-            tma_load_2d(sB + stage * B_BYTES, &tma_b, &full_bar[stage], kb * BK, n0);
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+              const int kx = (kb * KS + ks) * BK;
+              tma_load_2d(sA + stage * A_SLOT + ks * A_BYTES, &tma_a, &full_bar[stage], kx, m0);
+              tma_load_2d(sB + stage * B_SLOT + ks * B_BYTES, &tma_b, &full_bar[stage], kx, n0);
+            }
           }
           if (++stage == S) {
             stage = 0;
@@ -220,12 +236,13 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!wait(&full_bar[stage], phase, DEVERR_TMA_TIMEOUT)) goto done;
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          const uint32_t a_addr = smem_u32(sA + stage * A_SLOT);
+          const uint32_t b_addr = smem_u32(sB + stage * B_SLOT);
 #pragma unroll
-          for (int k = 0; k < BK / UK; ++k) {
-            const uint64_t ad = kmajor_sw128_desc(a_addr + k * UK);
-            const uint64_t bd = kmajor_sw128_desc(b_addr + k * UK);
+          for (int k = 0; k < KS * (BK / UK); ++k) {
+            const int ks = k / (BK / UK), kk = k % (BK / UK);
+            const uint64_t ad = kmajor_sw128_desc(a_addr + ks * A_BYTES + kk * UK);
+            const uint64_t bd = kmajor_sw128_desc(b_addr + ks * B_BYTES + kk * UK);
             const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
             if (PAIR) mma_i8_pair(d_tmem, ad, bd, IDESC, acc);
             else mma_i8(d_tmem, ad, bd, IDESC, acc);

@@ -164,7 +164,7 @@ __device__ __forceinline__ uint32_t pack4(uint2 a, uint2 b) {
 }
 
 template <int NST, bool BF16>
-__global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
+__global__ void __maxnreg__(104) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
                                                        const RotQuantParams p) {
   constexpr float kRoot = float(1 << NST);               // sqrt(G)
   constexpr float kQmaxRoot = 127.0f * float(1 << NST);  // 2032 for G = 256

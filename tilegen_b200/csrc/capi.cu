@@ -13,7 +13,7 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr int64_t kRotQuantMaxK = 32768;
-constexpr int kRotQuantRegs = 104;  // __maxnreg__ of rotquant_kernel
+constexpr int kRotQuantRegs = 96;  // __maxnreg__ of rotquant_kernel
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -163,7 +163,7 @@ int tg_rotate_quant(const void* x, int x_dtype, int64_t M, int64_t K, int group,
   }
   const uint32_t stage_bytes = uint32_t(threads) * 128u;
   // Ring depth: as deep as possible (up to 4) while the CTAs that the register
-  // budget allows per SM (104 registers a thread) still fit in shared memory.
+  // budget allows per SM (96 registers a thread) still fit in shared memory.
   int ctas = 65536 / (threads * kRotQuantRegs);
   ctas = ctas < 1 ? 1 : ctas;
   const uint32_t per_cta = 232448u / uint32_t(ctas) - 2048u - 1024u - uint32_t(3 * R) * 4u;

@@ -164,7 +164,7 @@ __device__ __forceinline__ uint32_t pack4(uint2 a, uint2 b) {
 }
 
 template <int NST, bool BF16>
-__global__ void __maxnreg__(104) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
+__global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
                                                        const RotQuantParams p) {
   constexpr float kRoot = float(1 << NST);               // sqrt(G)
   constexpr float kQmaxRoot = 127.0f * float(1 << NST);  // 2032 for G = 256
@@ -277,15 +277,19 @@ __global__ void __maxnreg__(104) rotquant_kernel(const __grid_constant__ CUtenso
       }
       // The next TMA into this slot must not overtake these generic accesses.
       fence_proxy_async_smem();
+      float am4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int jp = 0; jp < 8; ++jp) {
         bfly4x2(w2[0][jp], w2[1][jp], w2[2][jp], w2[3][jp]);
 #pragma unroll
-        for (int r = 0; r < 4; ++r) amax = absmax3(amax, w2[r][jp].x, w2[r][jp].y);
+        for (int r = 0; r < 4; ++r) am4[r] = absmax3(am4[r], w2[r][jp].x, w2[r][jp].y);
       }
+      amax = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
     } else {
+      float am4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int i = 0; i < 32; ++i) amax = absmax3(amax, vp[i].x, vp[i].y);
+      for (int i = 0; i < 32; ++i) am4[i & 3] = absmax3(am4[i & 3], vp[i].x, vp[i].y);
+      amax = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
     }
 
     // ---- row absmax -----------------------------------------------------------

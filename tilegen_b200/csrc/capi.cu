@@ -86,7 +86,17 @@ int launch_rotquant_t(const CUtensorMap& tm, const tg::RotQuantParams& p, int th
     return TG_ERR_CUDA;
   (void)occ_cache;
   const int64_t grid64 = std::min<int64_t>(p.nbatches, int64_t(sms) * occ);
-  kern<<<dim3(unsigned(grid64)), dim3(threads), smem, st>>>(tm, p);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(unsigned(grid64));
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, tm, p) != cudaSuccess) return TG_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
 }
 
@@ -223,7 +233,7 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid_units = tiles < units ? tiles : units;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.gridDim = dim3(unsigned(grid_units * (PAIR ? 2 : 1)));
   cfg.blockDim = dim3(tg::gemm::THREADS);
   cfg.dynamicSmemBytes = smem;
@@ -232,8 +242,12 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   attr[0].val.clusterDim.x = PAIR ? 2 : 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // Programmatic dependent launch: the prologue overlaps the previous kernel
+  // (the quantiser), the kernel waits for it before reading xq/xscale.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, kern, ta, tb, to, p) != cudaSuccess) return TG_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
 }

@@ -192,6 +192,17 @@ __device__ __forceinline__ uint32_t elect_one_lane() {
   return pred;
 }
 
+// ---------------------------------------------------------------- dependent launch
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream is still
+// running, once every CTA of that kernel has executed launch_dependents (or
+// exited); its threads must execute wait before reading anything the previous
+// kernel writes.  Both are no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- clusters (CTA pairs)
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -167,6 +167,10 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   if (PAIR) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  // Everything above overlaps the tail of the kernel that produced xq/xscale
+  // (when launched as its programmatic dependent); nothing below may read them
+  // before it has completed.
+  pdl_wait();
 
   // Bounded wait that also gives up as soon as another role has given up.
   auto wait = [&](uint64_t* bar, uint32_t parity, unsigned int err) -> bool {

@@ -150,7 +150,9 @@ __device__ __forceinline__ void unpack8(const uint4 w, float2* f) {
 // (ties to even) and leaves it in the low mantissa bits; the lower clamp also
 // maps NaN to -128 as fmaxf does in the reference.  No upper clamp is needed:
 // |x| <= absmax and inv = 1/(sqrt(G)*scale) with scale >= absmax/(127*sqrt(G))
-// bound x*inv by 127*(1+2^-22), which rounds to 127.
+// bound x*inv by 127*(1+2^-22), which rounds to 127.  The clamp also keeps the
+// multiply and the add apart: with nothing between them ptxas fuses the f32x2
+// mul.rn and add.rn into one fma, which rounds once and differs at exact ties.
 __device__ __forceinline__ uint2 code_bits2(float2 x, float2 inv2) {
   float2 t = mul2(x, inv2);
   t.x = fmaxf(t.x, -128.0f);
@@ -189,6 +191,11 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
   }
   for (int i = tid; i < 3 * R; i += blockDim.x) rowmax[i] = 0u;
   __syncthreads();
+  // Let the next kernel in the stream (the GEMM) be scheduled as SMs free up;
+  // it waits for this grid's completion before reading the codes.  Then wait
+  // for whatever produced x before the first load.
+  pdl_launch_dependents();
+  pdl_wait();
 
   const int64_t first = blockIdx.x;
   const int64_t step = gridDim.x;

@@ -1,0 +1,67 @@
+"""Row-sharded linear on 2 GPUs with NCCL: each rank runs the kernels on its rows,
+gather_rows all-gathers the blocks; the result equals the single-GPU output bit for
+bit.  Skipped when fewer than two GPUs are visible."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, m, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from tilegen_b200.kernels.int8_convrot import quantize_convrot
+    from tilegen_b200.quant import int8_matmul_dequant_chunked, quantize_convrot_weight
+    from tilegen_b200.sharding import gather_rows, int8_convrot_linear_local, local_rows
+    from tilegen_b200.synthetic import gaussian_weight, outlier_activations
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        x = outlier_activations(m, 5120, seed=0, dtype=torch.bfloat16).to(dev)
+        wq, ws = quantize_convrot_weight(gaussian_weight(1024, 5120, seed=1, dtype=torch.bfloat16).to(dev), 256)
+        y = gather_rows(int8_convrot_linear_local(local_rows(x, world, rank), wq, ws, None, torch.bfloat16), m)
+        xq, xs = quantize_convrot(x, 256, backend="fht")
+        ref = int8_matmul_dequant_chunked(xq, xs, wq, ws, None, torch.bfloat16)
+        q.put((rank, bool(torch.equal(y, ref)), tuple(y.shape)))
+    except Exception as e:  # report, never hang
+        q.put((rank, False, f"{type(e).__name__}: {e}"[:200]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("m", [4096, 8190])
+def test_sharded_linear_equals_single_gpu_nccl(m):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, m, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung")
+    res = sorted(q.get(timeout=10) for _ in procs)
+    assert all(r[1] for r in res), res

@@ -146,7 +146,8 @@ int tg_rotate_quant(const void* x, int x_dtype, int64_t M, int64_t K, int group,
   if (!x || !q || !scale) return TG_ERR_INVALID_ARG;
   if (!aligned16(x) || !aligned16(q) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return TG_ERR_MISALIGNED;
   const int cpr = int(K / 64);
-  if (M * int64_t(cpr) >= (int64_t(1) << 31)) return TG_ERR_UNSUPPORTED;
+  // 32-bit line and batch indices in the kernel (with up to 8 rows of slack).
+  if ((M + 8) * int64_t(cpr) >= (int64_t(1) << 31)) return TG_ERR_UNSUPPORTED;
 
   // Rows per batch: the fewest that fill whole warps to within 5 %.
   int R = 1;

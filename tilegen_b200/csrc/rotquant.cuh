@@ -174,18 +174,33 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(p.stages) * p.stage_bytes);
-  unsigned* rowmax = reinterpret_cast<unsigned*>(full + p.stages);  // [3][R]
+  // Launch-constant values, read once (32-bit: the host guarantees
+  // M * K / 64 < 2^31, so batch and line indices fit).
+  const int stages = p.stages;
+  const uint32_t stage_bytes = p.stage_bytes;
+  const int R = p.rows_per_batch;
+  const int cpr = p.cpr;
+  const int K = p.K;
+  const int M = int(p.M);
+  const int nbatches = int(p.nbatches);
+  const int seg = p.seg;
+  const int active_threads = p.active;
+  const int boxes = p.boxes;
+  const int box_lines = p.box_lines;
+  int8_t* const qout = p.q;
+  float* const sout = p.scale;
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(stages) * stage_bytes);
+  unsigned* rowmax = reinterpret_cast<unsigned*>(full + stages);  // [3][R]
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int R = p.rows_per_batch;
 
   if (tid == 0) {
     prefetch_tmap(&tmx);
-    for (int s = 0; s < p.stages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
     abort_flag = 0;
   }
@@ -197,44 +212,59 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
   pdl_launch_dependents();
   pdl_wait();
 
-  const int64_t first = blockIdx.x;
-  const int64_t step = gridDim.x;
-  const uint32_t batch_bytes = uint32_t(p.boxes) * uint32_t(p.box_lines) * 128u;
+  const int first = blockIdx.x;
+  const int step = gridDim.x;
+  const uint32_t batch_bytes = uint32_t(boxes) * uint32_t(box_lines) * 128u;
 
-  auto issue = [&](int64_t batch, int s) {
+  auto issue = [&](int batch, int s) {
     mbar_arrive_expect_tx(&full[s], batch_bytes);
-    uint8_t* dst = smem + size_t(s) * p.stage_bytes;
-    const int64_t line0 = batch * int64_t(p.active);
-    for (int b = 0; b < p.boxes; ++b)
-      tma_load_2d(dst + size_t(b) * p.box_lines * 128, &tmx, &full[s], 0, int(line0 + int64_t(b) * p.box_lines));
+    uint8_t* dst = smem + size_t(s) * stage_bytes;
+    const int line0 = batch * active_threads;
+    for (int b = 0; b < boxes; ++b)
+      tma_load_2d(dst + size_t(b) * box_lines * 128, &tmx, &full[s], 0, line0 + b * box_lines);
   };
 
   if (tid == 0) {
-    for (int s = 0; s < p.stages; ++s) {
-      const int64_t b = first + int64_t(s) * step;
-      if (b < p.nbatches) issue(b, s);
+    for (int s = 0; s < stages; ++s) {
+      const int b = first + s * step;
+      if (b < nbatches) issue(b, s);
     }
   }
 
-  const bool active = tid < p.active;
-  const int row_local = tid / p.cpr;
-  const int chunk = tid - row_local * p.cpr;
+  const bool active = tid < active_threads;
+  const int row_local = tid / cpr;
+  const int chunk = tid - row_local * cpr;
+  // This thread's line in a ring slot: 128 bytes, 16-byte units swizzled by
+  // (line & 7) = (lane & 7); folding that into the base turns each unit's
+  // address into base ^ (unit * 16).
+  const uint32_t line_off = uint32_t(tid) * 128u + (uint32_t(lane & 7) << 4);
+  // Exchange area: the warp's own 4 KB of the slot, rows of 80 bytes (lane L
+  // writes row L; the reader of quad gq, position qd reads rows 4gq..4gq+3 at
+  // column qd).  Per quarter warp, writes hit 16-byte units 5L + b and reads
+  // 4gq + 5c + qd (mod 8): eight distinct units each, so no bank conflicts.
+  const uint32_t xw_off = uint32_t(warp) * 4096u + uint32_t(lane) * 80u;
+  const uint32_t xr_off = uint32_t(warp) * 4096u + uint32_t(lane >> 2) * 320u + uint32_t(lane & 3) * 16u;
+  // Codes of this thread: NST == 4 writes one 16-value block per output
+  // quarter of its group (stride 64), else its own 64 contiguous values.
+  const int code_off = NST == 4 ? (chunk >> 2) * 256 + (chunk & 3) * 16 : chunk * 64;
 
-  int it = 0;
-  for (int64_t batch = first; batch < p.nbatches; batch += step, ++it) {
-    const int s = it % p.stages;
-    const uint32_t parity = uint32_t(it / p.stages) & 1u;
+  int s = 0;
+  uint32_t parity = 0;
+  int rm_cur = 0;  // rowmax slot of this batch (triple-buffered)
+  int abort_batch = nbatches;
+  for (int batch = first; batch < nbatches; batch += step) {
+    abort_batch = batch;
     if (!mbar_wait(&full[s], parity, DEVERR_TMA_TIMEOUT)) abort_flag = 1;
-    uint8_t* buf = smem + size_t(s) * p.stage_bytes;
+    uint8_t* buf = smem + size_t(s) * stage_bytes;
 
-    // ---- own line (64 values) from the swizzled stage buffer ------------------
+    // ---- own line (64 values) from the swizzled ring slot ------------------
     float2 vp[32];
     {
-      const uint32_t line = uint32_t(tid);
-      const uint8_t* lp = buf + line * 128u;
+      const uint8_t* lp = buf + line_off;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        const uint4 w = *reinterpret_cast<const uint4*>(lp + ((uint32_t(c) ^ (line & 7u)) << 4));
+        const uint4 w = *reinterpret_cast<const uint4*>(
+            reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(lp) ^ uintptr_t(c << 4)));
         unpack8<BF16>(w, &vp[4 * c]);
       }
     }
@@ -242,43 +272,26 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
     if (NST >= 2) stage1_64(vp);
     if (NST >= 3) stage2_64(vp);
 
-    float amax = 0.0f;
+    float amax;
     float2 w2[4][8];  // NST == 4 only: [input c][column pair] of this thread's block
     if (NST == 4) {
       // Swap 16-value blocks among the four threads of a group through this
-      // warp's 4 KB slice of the stage buffer (its own lines, already read).
-      // Row r of the slice is written by lane r; 16-byte chunks are XOR
-      // swizzled with f(r) = ((r&3)<<1) | ((r>>2)&1) so that both the writes
-      // and the transposed reads hit 8 distinct chunk positions per quarter
-      // warp.  Two rounds of 8 columns fit the 4 KB slice.
+      // warp's (already consumed) slice of the slot, four values of each
+      // block per round, so that afterwards each thread holds one 16-wide
+      // column block for all four inputs of the last butterfly, in input order.
       __syncwarp();
-      uint8_t* xb = buf + size_t(warp) * 4096u;
-      const int gq = lane >> 2;
-      const int qd = lane & 3;
-      const uint32_t fw = (uint32_t(qd) << 1) | (uint32_t(gq) & 1u);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      for (int r = 0; r < 4; ++r) {
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-#pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            const int o = 8 * b + 4 * half + 2 * jj;  // pair index of value 16b + 8half + 4jj
-            *reinterpret_cast<float4*>(xb + lane * 128 + ((uint32_t(2 * b + jj) ^ fw) << 4)) =
-                make_float4(vp[o].x, vp[o].y, vp[o + 1].x, vp[o + 1].y);
-          }
-        }
+        for (int b = 0; b < 4; ++b)
+          *reinterpret_cast<float4*>(buf + xw_off + b * 16) =
+              make_float4(vp[8 * b + 2 * r].x, vp[8 * b + 2 * r].y, vp[8 * b + 2 * r + 1].x, vp[8 * b + 2 * r + 1].y);
         __syncwarp();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint32_t fr = (uint32_t(c) << 1) | (uint32_t(gq) & 1u);
-#pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            const float4 t = *reinterpret_cast<const float4*>(xb + (4 * gq + c) * 128 +
-                                                              ((uint32_t(2 * qd + jj) ^ fr) << 4));
-            const int jp = 4 * half + 2 * jj;
-            w2[c][jp] = make_float2(t.x, t.y);
-            w2[c][jp + 1] = make_float2(t.z, t.w);
-          }
+          const float4 t = *reinterpret_cast<const float4*>(buf + xr_off + c * 80);
+          w2[c][2 * r] = make_float2(t.x, t.y);
+          w2[c][2 * r + 1] = make_float2(t.z, t.w);
         }
         __syncwarp();
       }
@@ -300,30 +313,31 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
     }
 
     // ---- row absmax -----------------------------------------------------------
-    for (int o = 1; o < p.seg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    unsigned* rm = rowmax + (it % 3) * R;
-    if (active && (lane & (p.seg - 1)) == 0) atomicMax(&rm[row_local], __float_as_uint(amax));
+    for (int o = 1; o < seg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    unsigned* rm = rowmax + rm_cur * R;
+    if (active && (lane & (seg - 1)) == 0) atomicMax(&rm[row_local], __float_as_uint(amax));
     __syncthreads();
     if (abort_flag) break;
 
     // Slot s is free again (every thread has read it): refill it.
     if (tid == 0) {
-      const int64_t nb = batch + int64_t(p.stages) * step;
-      if (nb < p.nbatches) issue(nb, s);
+      const int nb = batch + stages * step;
+      if (nb < nbatches) issue(nb, s);
     }
-    // Slot (it+2)%3 was last read before the previous barrier and is next
-    // written after the following one.
-    if (tid < R) rowmax[((it + 2) % 3) * R + tid] = 0u;
+    // The slot after next was last read before the previous barrier and is
+    // next written after the following one.
+    const int rm_clear = rm_cur == 0 ? 2 : rm_cur - 1;
+    if (tid < R) rowmax[rm_clear * R + tid] = 0u;
 
-    const int64_t row = batch * R + row_local;
-    if (active && row < p.M) {
+    const int row = batch * R + row_local;
+    if (active && row < M) {
       const float am = __uint_as_float(rm[row_local]);
       const float sc = fmaxf(__fdiv_rn(am, kQmaxRoot), 1e-30f);
-      if (chunk == 0) p.scale[row] = sc;
+      if (chunk == 0) sout[row] = sc;
       const float inv = __fdiv_rn(1.0f, __fmul_rn(sc, kRoot));
       const float2 inv2 = make_float2(inv, inv);
+      int8_t* qp = qout + size_t(row) * size_t(K) + code_off;
       if (NST == 4) {
-        int8_t* qp = p.q + row * int64_t(p.K) + (chunk >> 2) * 256 + (chunk & 3) * 16;
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
           uint32_t wd[4];
@@ -333,7 +347,6 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
           *reinterpret_cast<uint4*>(qp + r * 64) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
         }
       } else {
-        int8_t* qp = p.q + row * int64_t(p.K) + chunk * 64;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t wd[4];
@@ -346,13 +359,22 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
         }
       }
     }
+    rm_cur = rm_cur == 2 ? 0 : rm_cur + 1;
+    if (++s == stages) {
+      s = 0;
+      parity ^= 1u;
+    }
   }
 
   // A wait gave up: let the copies still in flight land before the CTA exits.
+  // The loop left at a batch whose slot s (phase `parity`) is next; the loads
+  // in flight are that batch's and the following stages - 1 batches' (slots
+  // s, s+1, ... wrapping to the other phase).
   if (abort_flag && tid == 0) {
-    for (int k = it; k < it + p.stages; ++k) {
-      const int64_t b = first + int64_t(k) * step;
-      if (b < p.nbatches) mbar_wait(&full[k % p.stages], uint32_t(k / p.stages) & 1u, DEVERR_TMA_TIMEOUT);
+    for (int k = 0; k < stages; ++k) {
+      const int slot = (s + k) % stages;
+      const uint32_t par = (s + k < stages) ? parity : (parity ^ 1u);
+      if (abort_batch + k * step < nbatches) mbar_wait(&full[slot], par, DEVERR_TMA_TIMEOUT);
     }
   }
 }

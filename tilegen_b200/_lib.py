@@ -105,6 +105,12 @@ def lib() -> ctypes.CDLL:
         L.tg_set_gemm_config.restype = i32
         L.tg_device_status.argtypes = [i32, ctypes.POINTER(ctypes.c_uint32), i32]
         L.tg_device_status.restype = i32
+        L.tg_int8_gemm_dequant_splitk.argtypes = [p, p, p, p, i64, p, i32, i64, i64, i64, i32, p, p,
+                                                  ctypes.c_size_t, p]
+        L.tg_int8_gemm_dequant_splitk.restype = i32
+        L.tg_int8_gemm_dequant_splitk_workspace.argtypes = [i64, i64]
+        L.tg_int8_gemm_dequant_splitk_workspace.restype = ctypes.c_size_t
+        L.tg_int8_gemm_dequant_splitk_max_m.restype = i64
         _lib = L
     return _lib
 

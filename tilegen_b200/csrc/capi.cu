@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "gemm_i8.cuh"
+#include "gemm_splitk.cuh"
 #include "rotquant.cuh"
 
 namespace {
@@ -435,5 +436,158 @@ int tg_device_status(int device, uint32_t* bits, int clear) {
   *bits = v;
   return v ? TG_ERR_DEVICE_TIMEOUT : TG_OK;
 }
+
+}  // extern "C"
+
+// ------------------------------------------------------------ small-M GEMM
+namespace {
+
+size_t round256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// The argument checks of tg_int8_gemm_dequant (M == 0 passes).
+int check_gemm_args(const int8_t* xq, const float* xscale, const int8_t* wq, const float* wscale,
+                    int64_t wscale_numel, const void* bias, int bias_dtype, int64_t M, int64_t N, int64_t K,
+                    int out_dtype, const void* out) {
+  if (M < 0 || N <= 0 || K <= 0) return TG_ERR_INVALID_ARG;
+  if (out_dtype != TG_DT_F32 && out_dtype != TG_DT_F16 && out_dtype != TG_DT_BF16) return TG_ERR_INVALID_ARG;
+  if (bias && bias_dtype != TG_DT_F32 && bias_dtype != TG_DT_F16 && bias_dtype != TG_DT_BF16)
+    return TG_ERR_INVALID_ARG;
+  if (wscale_numel != 1 && wscale_numel != N) return TG_ERR_INVALID_ARG;
+  const int esz = out_dtype == TG_DT_F32 ? 4 : 2;
+  if (K % 16 != 0 || (N * esz) % 16 != 0) return TG_ERR_UNSUPPORTED;
+  if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31) || K >= (int64_t(1) << 31)) return TG_ERR_UNSUPPORTED;
+  if (M == 0) return TG_OK;
+  if (!xq || !xscale || !wq || !wscale || !out) return TG_ERR_INVALID_ARG;
+  if (!aligned16(xq) || !aligned16(wq) || !aligned16(out)) return TG_ERR_MISALIGNED;
+  if ((reinterpret_cast<uintptr_t>(xscale) & 3u) || (reinterpret_cast<uintptr_t>(wscale) & 3u))
+    return TG_ERR_MISALIGNED;
+  return TG_OK;
+}
+
+// Workspace of the split-K GEMM: [count: ceil(N/128) u32 | acc: M x N int32],
+// each part 256-byte aligned.
+struct SplitKWs {
+  size_t count, acc, total;
+};
+SplitKWs splitk_ws(int64_t M, int64_t N) {
+  SplitKWs w;
+  const int64_t tiles = (N + tg::splitk::BNW - 1) / tg::splitk::BNW;
+  w.count = 0;
+  w.acc = round256(size_t(tiles) * 4);
+  w.total = w.acc + round256(size_t(M) * size_t(N) * 4);
+  return w;
+}
+
+template <int MPAD, int OUT, bool HAS_BIAS>
+int launch_splitk_t(const CUtensorMap& tw, const CUtensorMap& tx, const tg::SplitKParams& p, int tiles, int dev,
+                    cudaStream_t st) {
+  static uint32_t attr_done[kMaxDevices];
+  constexpr uint32_t smem = tg::splitk::smem_bytes(MPAD);
+  auto kern = tg::gemm_i8_splitk_kernel<MPAD, OUT, HAS_BIAS>;
+  if (!ensure_smem_attr(kern, dev, smem, attr_done)) return TG_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(unsigned(p.slices), unsigned(tiles));
+  cfg.blockDim = dim3(tg::splitk::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, tw, tx, p) != cudaSuccess) return TG_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
+}
+
+template <int MPAD>
+int launch_splitk_m(const CUtensorMap& tw, const CUtensorMap& tx, const tg::SplitKParams& p, int tiles,
+                    int out_dtype, bool hb, int dev, cudaStream_t st) {
+  switch (out_dtype) {
+    case TG_DT_F32: return hb ? launch_splitk_t<MPAD, 0, true>(tw, tx, p, tiles, dev, st)
+                              : launch_splitk_t<MPAD, 0, false>(tw, tx, p, tiles, dev, st);
+    case TG_DT_F16: return hb ? launch_splitk_t<MPAD, 1, true>(tw, tx, p, tiles, dev, st)
+                              : launch_splitk_t<MPAD, 1, false>(tw, tx, p, tiles, dev, st);
+    default: return hb ? launch_splitk_t<MPAD, 2, true>(tw, tx, p, tiles, dev, st)
+                       : launch_splitk_t<MPAD, 2, false>(tw, tx, p, tiles, dev, st);
+  }
+}
+
+// The split-K launch over a zero-initialised scratch (count, acc), shared by
+// the workspace entry point and any other caller that owns such scratch.
+int splitk_launch(const int8_t* xq, const float* xscale, const int8_t* wq, const float* wscale,
+                  int64_t wscale_numel, const void* bias, int bias_dtype, int64_t M, int64_t N, int64_t K,
+                  int out_dtype, void* out, uint32_t* count, int32_t* acc, void* stream) {
+  using namespace tg::splitk;
+  int dev;
+  DeviceInfo info;
+  if (!current_device(&dev, &info)) return TG_ERR_CUDA;
+  const int mpad = int((M + 15) / 16 * 16);
+  const int tiles = int((N + BNW - 1) / BNW);
+  const int k_blocks = int((K + BK - 1) / BK);
+  // About two CTAs per SM stream the weight: split K until tiles x slices
+  // reaches that, keeping every slice non-empty.
+  int slices = (2 * info.sms + tiles - 1) / tiles;
+  slices = slices < 1 ? 1 : (slices > k_blocks ? k_blocks : slices);
+  const int kb_per = (k_blocks + slices - 1) / slices;
+  slices = (k_blocks + kb_per - 1) / kb_per;
+
+  CUtensorMap tw, tx;
+  if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, uint64_t(K), uint64_t(N), uint64_t(K), BK, BNW,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return TG_ERR_CUDA;
+  if (!make_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, uint64_t(K), uint64_t(M), uint64_t(K), BK,
+                    uint32_t(mpad), CU_TENSOR_MAP_SWIZZLE_128B))
+    return TG_ERR_CUDA;
+  tg::SplitKParams p;
+  p.xscale = xscale;
+  p.wscale = wscale;
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.wscale_bcast = wscale_numel == 1 ? 1 : 0;
+  p.M = int(M);
+  p.N = int(N);
+  p.K = int(K);
+  p.k_blocks = k_blocks;
+  p.kb_per_slice = kb_per;
+  p.slices = slices;
+  p.acc = acc;
+  p.count = count;
+  p.out = out;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool hb = bias != nullptr;
+  switch (mpad) {
+    case 16: return launch_splitk_m<16>(tw, tx, p, tiles, out_dtype, hb, dev, st);
+    case 32: return launch_splitk_m<32>(tw, tx, p, tiles, out_dtype, hb, dev, st);
+    case 48: return launch_splitk_m<48>(tw, tx, p, tiles, out_dtype, hb, dev, st);
+    default: return launch_splitk_m<64>(tw, tx, p, tiles, out_dtype, hb, dev, st);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t tg_int8_gemm_dequant_splitk_workspace(int64_t M, int64_t N) {
+  if (M < 0 || N < 0) return 0;
+  return splitk_ws(M, N).total;
+}
+
+int tg_int8_gemm_dequant_splitk(const int8_t* xq, const float* xscale, const int8_t* wq, const float* wscale,
+                                int64_t wscale_numel, const void* bias, int bias_dtype, int64_t M, int64_t N,
+                                int64_t K, int out_dtype, void* out, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  const int chk = check_gemm_args(xq, xscale, wq, wscale, wscale_numel, bias, bias_dtype, M, N, K, out_dtype, out);
+  if (chk != TG_OK || M == 0) return chk;
+  if (M > tg::splitk::M_MAX) return TG_ERR_UNSUPPORTED;
+  if (!workspace) return TG_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u) return TG_ERR_MISALIGNED;
+  const SplitKWs L = splitk_ws(M, N);
+  if (workspace_bytes < L.total) return TG_ERR_INVALID_ARG;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  return splitk_launch(xq, xscale, wq, wscale, wscale_numel, bias, bias_dtype, M, N, K, out_dtype, out,
+                       reinterpret_cast<uint32_t*>(ws + L.count), reinterpret_cast<int32_t*>(ws + L.acc), stream);
+}
+
+int64_t tg_int8_gemm_dequant_splitk_max_m(void) { return tg::splitk::M_MAX; }
 
 }  // extern "C"

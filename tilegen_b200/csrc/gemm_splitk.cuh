@@ -1,0 +1,270 @@
+// Small-M INT8 GEMM with the dequantising epilogue (sm_100a), for M <= 64
+// activation rows (decode / preview steps):
+//
+//   out[m,n] = ((float(sum_k xq[m,k]*wq[n,k]) * xscale[m]) * wscale[n]) + bias[n]
+//
+// the arithmetic of tilegen/quant/int8_ops.py:22-70, as in gemm_i8.cuh.  With
+// few rows the work is streaming the weight (N*K bytes) once; the 128-row
+// tiles of gemm_i8.cuh would put only N/256 CTAs on that stream.  Here:
+//  * The roles of the operands are swapped: a 128-row tile of the WEIGHT is
+//    the UMMA M operand and the (zero-padded) activation rows are UMMA N
+//    (MPAD = 16..64), so D[n, m] accumulates in a 128-lane x MPAD-column
+//    TMEM tile (tcgen05 kind::i8, int32).
+//  * K is split: CTA (s, t) multiplies column tile t over k-blocks
+//    [s*kb_per_slice, ...), so that N/128 x slices CTAs stream the weight
+//    from all SMs.
+//  * Each CTA adds its int32 partial tile into an [M, N] int32 scratch
+//    accumulator with red.global.add (integer addition: exact and
+//    order-independent), then counts itself in count[t].  The CTA that brings
+//    count[t] to `slices` reads the finished sums, applies the dequantisation
+//    (one rounding per operation, as the reference), stores the output, and
+//    writes zeros back over its accumulator tile and counter.  The scratch is
+//    therefore all-zero between launches; it must be zero before the first.
+// Roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
+// warps 2-5 epilogue.  Every wait is bounded (common.cuh).
+#pragma once
+
+#include "common.cuh"
+#include "gemm_i8.cuh"
+
+namespace tg {
+
+namespace splitk {
+constexpr int BNW = 128;                 // weight rows per tile (UMMA M)
+constexpr int BK = 128;                  // bytes of K per k-block
+constexpr int UK = 32;                   // K per tcgen05.mma kind::i8
+constexpr uint32_t W_BYTES = BNW * BK;   // 16 KB
+constexpr int THREADS = 192;
+constexpr int M_MAX = 64;
+constexpr int STAGES = 4;
+__host__ __device__ constexpr uint32_t x_bytes(int mpad) { return uint32_t(mpad) * BK; }
+__host__ __device__ constexpr uint32_t stage_bytes(int mpad) { return W_BYTES + x_bytes(mpad); }
+__host__ __device__ constexpr uint32_t smem_bytes(int mpad) { return STAGES * stage_bytes(mpad) + 1024; }
+}  // namespace splitk
+
+struct SplitKParams {
+  const float* xscale;
+  const float* wscale;
+  const void* bias;
+  int bias_dtype;
+  int wscale_bcast;
+  int M, N, K;
+  int k_blocks;      // ceil(K / 128)
+  int kb_per_slice;  // k-blocks per CTA
+  int slices;        // CTAs per column tile (gridDim.x)
+  int32_t* acc;      // [M, N] partial sums: zero on entry, zero on exit
+  uint32_t* count;   // [ceil(N / 128)] finished slices: zero on entry, zero on exit
+  void* out;         // [M, N] of OUT
+};
+
+// MPAD: activation rows padded to a multiple of 16 (the UMMA N); OUT: tg_dtype.
+template <int MPAD, int OUT, bool HAS_BIAS>
+__global__ void __launch_bounds__(splitk::THREADS, 1)
+    gemm_i8_splitk_kernel(const __grid_constant__ CUtensorMap tma_w, const __grid_constant__ CUtensorMap tma_x,
+                          const SplitKParams p) {
+  using namespace splitk;
+  static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= M_MAX, "padded rows");
+  constexpr uint32_t XB = x_bytes(MPAD);
+  constexpr uint32_t TX_BYTES = W_BYTES + XB;
+  constexpr uint32_t TMEM_COLS = MPAD <= 32 ? 32 : 64;
+  constexpr uint32_t IDESC = gemm::idesc(BNW, MPAD);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sW = smem;
+  uint8_t* sX = smem + STAGES * W_BYTES;
+
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+  __shared__ int last_slice;
+  __shared__ int issued;  // TMA loads the producer issued
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int slice = blockIdx.x;
+  const int tile = blockIdx.y;
+  const int n0 = tile * BNW;
+  const int kb0 = slice * p.kb_per_slice;
+  const int kb1 = min(kb0 + p.kb_per_slice, p.k_blocks);
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tma_w);
+    prefetch_tmap(&tma_x);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&tfull_bar, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+    issued = 0;
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+  // Overlaps the end of the kernel that produced xq/xscale when launched as
+  // its programmatic dependent; nothing below reads them before it completed.
+  pdl_wait();
+
+  auto wait = [&](uint64_t* bar, uint32_t parity, unsigned int err) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (;;) {
+      for (int i = 0; i < 32; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+      if (abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(&g_device_status, err);
+        abort_flag = 1;
+        return false;
+      }
+    }
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int n_issued = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait(&empty_bar[stage], phase ^ 1u, DEVERR_PIPE_TIMEOUT)) break;
+        mbar_arrive_expect_tx(&full_bar[stage], TX_BYTES);
+        tma_load_2d(sW + stage * W_BYTES, &tma_w, &full_bar[stage], kb * BK, n0);
+        tma_load_2d(sX + stage * XB, &tma_x, &full_bar[stage], kb * BK, 0);
+        ++n_issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      issued = n_issued;
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!wait(&full_bar[stage], phase, DEVERR_TMA_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t w_addr = smem_u32(sW + stage * W_BYTES);
+        const uint32_t x_addr = smem_u32(sX + stage * XB);
+#pragma unroll
+        for (int k = 0; k < BK / UK; ++k)
+          mma_i8(tmem_base, gemm::kmajor_sw128_desc(w_addr + k * UK), gemm::kmajor_sw128_desc(x_addr + k * UK),
+                 IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
+        mma_commit(&empty_bar[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) mma_commit(&tfull_bar);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int et = threadIdx.x - 64;  // 0..127
+    const int quarter = warp & 3;     // TMEM lanes [32*quarter, +32)
+    const int n = n0 + quarter * 32 + lane;
+    // Warp-uniform: tcgen05.ld below is executed by all 32 lanes or none.
+    const bool got = __all_sync(0xffffffffu, wait(&tfull_bar, 0u, DEVERR_MMA_TIMEOUT));
+    if (got) {
+      tc_fence_after();
+      uint32_t v[MPAD];
+#pragma unroll
+      for (int h = 0; h < MPAD / 16; ++h)
+        tmem_ld_32x32b_x16(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(h * 16),
+                           *reinterpret_cast<uint32_t(*)[16]>(&v[h * 16]));
+      tmem_wait_ld();
+      // Coalesced over the warp: 32 consecutive n of one row m per step.
+      if (n < p.N) {
+        int32_t* a = p.acc + n;
+#pragma unroll
+        for (int m = 0; m < MPAD; ++m)
+          if (m < p.M) atomicAdd(a + size_t(m) * p.N, static_cast<int32_t>(v[m]));
+      }
+      __threadfence();
+    }
+    named_barrier(1, 128);
+    // Counted even after a wait gave up (that slice then adds nothing), so
+    // the last slice still returns the scratch to zero; the status word
+    // reports the failure.
+    if (et == 0) last_slice = atomicAdd(p.count + tile, 1u) == uint32_t(p.slices - 1);
+    named_barrier(1, 128);
+    if (last_slice) {
+      // Every slice's additions are in: dequantise this column tile and put
+      // the accumulator and the counter back to zero.
+      __threadfence();
+      if (n < p.N) {
+        const float ws = p.wscale[p.wscale_bcast ? 0 : n];
+        float bs = 0.0f;
+        if (HAS_BIAS) {
+          if (p.bias_dtype == TG_DT_F32) bs = static_cast<const float*>(p.bias)[n];
+          else if (p.bias_dtype == TG_DT_F16) bs = __half2float(static_cast<const __half*>(p.bias)[n]);
+          else bs = __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n]);
+        }
+        // Rows are finished 16 at a time: their sums are all loaded before any
+        // is used, so the L2 latencies overlap instead of adding up.
+        const size_t stride = size_t(p.N);
+        int32_t* arow = p.acc + n;
+        char* orow = static_cast<char*>(p.out) + size_t(n) * (OUT == 0 ? 4 : 2);
+        const size_t ostride = stride * (OUT == 0 ? 4 : 2);
+#pragma unroll
+        for (int m0 = 0; m0 < MPAD; m0 += 16) {
+          int32_t a[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (m0 + j < p.M) a[j] = __ldcg(arow + j * stride);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if (m0 + j < p.M) {
+              __stcg(arow + j * stride, 0);
+              float r = __int2float_rn(a[j]);
+              r = __fmul_rn(r, __ldg(p.xscale + m0 + j));
+              r = __fmul_rn(r, ws);
+              if (HAS_BIAS) r = __fadd_rn(r, bs);
+              char* o = orow + j * ostride;
+              if (OUT == 0) *reinterpret_cast<float*>(o) = r;
+              else if (OUT == 1) *reinterpret_cast<__half*>(o) = __float2half_rn(r);
+              else *reinterpret_cast<__nv_bfloat16*>(o) = __float2bfloat16_rn(r);
+            }
+          }
+          arow += 16 * stride;
+          orow += 16 * ostride;
+        }
+      }
+      named_barrier(1, 128);
+      if (et == 0) p.count[tile] = 0u;
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  // A wait gave up: let the loads still in flight (at most the last STAGES
+  // issued, one per slot) land before the CTA exits.
+  if (abort_flag && threadIdx.x == 0) {
+    for (int i = max(0, issued - STAGES); i < issued; ++i)
+      mbar_wait(&full_bar[i % STAGES], uint32_t(i / STAGES) & 1u, DEVERR_TMA_TIMEOUT);
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace tg

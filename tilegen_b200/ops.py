@@ -4,7 +4,8 @@
 caching allocator and enqueue the sm_100a kernels on the current stream of the
 input's device.  They never fall back to another implementation: an input the
 kernels do not handle raises ``ValueError``, a CUDA failure raises
-``TileGenError``.
+``TileGenError``.  ``int8_gemm_dequant`` with few rows (see ``SPLITK_MAX_M``)
+uses the split-K kernel and a cached, self-clearing scratch per (device, stream).
 
 The same two functions are registered as ``torch.ops.tilegen.rotate_quant`` and
 ``torch.ops.tilegen.int8_gemm_dequant`` (with fake implementations, so they
@@ -111,10 +112,38 @@ def int8_gemm_dequant(xq: torch.Tensor, xscale: torch.Tensor, wq: torch.Tensor, 
         bias = b
         b_ptr, b_code = b.data_ptr(), _DTYPE_CODE[b.dtype]
     out = torch.empty((m, n), dtype=out_dtype, device=dev)
-    if m:
+    if 0 < m <= SPLITK_MAX_M and (m <= 16 or k >= 8192):
+        work = _splitk_workspace(dev, m, n)
+        _call("tg_int8_gemm_dequant_splitk", dev, xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),
+              ws.numel(), b_ptr, b_code, m, n, k, _DTYPE_CODE[out_dtype], out.data_ptr(), work.data_ptr(),
+              work.numel())
+    elif m:
         _call("tg_int8_gemm_dequant", dev, xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),
               ws.numel(), b_ptr, b_code, m, n, k, _DTYPE_CODE[out_dtype], out.data_ptr())
     return out
+
+
+# int8_gemm_dequant takes the split-K kernel (tg_int8_gemm_dequant_splitk) for
+# M <= 16, and up to SPLITK_MAX_M rows when K >= 8192: measured on B200 at the
+# DiT shapes, the tiled kernel is faster from M ~ 32 unless K is long.
+# 0 sends every M to the tiled kernel.
+SPLITK_MAX_M = 64
+
+# Split-K scratch, one per (device, stream): zero-filled when created and left
+# zero by every call, so it is reused as is; it only grows.
+_SPLITK_WS: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _splitk_workspace(dev: torch.device, m: int, n: int) -> torch.Tensor:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+    need = int(_lib.lib().tg_int8_gemm_dequant_splitk_workspace(m, n))
+    ws = _SPLITK_WS.get(key)
+    if ws is None or ws.numel() < need:
+        # The caching allocator returns 512-byte aligned blocks (256 needed).
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+        _SPLITK_WS[key] = ws
+    return ws
 
 
 # ---------------------------------------------------------------- custom ops

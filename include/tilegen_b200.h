@@ -111,6 +111,28 @@ size_t tg_int8_gemm_dequant_splitk_workspace(int64_t M, int64_t N);
 int64_t tg_int8_gemm_dequant_splitk_max_m(void);
 
 /*
+ * tg_int8_gemm_dequant_splitk for callers that cannot allocate device memory:
+ * a plugin running inside a host application that owns all GPU memory through
+ * its own allocator, or a serving process whose memory is fully reserved up
+ * front, where a cudaMalloc would fail or stall the device.  It takes no
+ * workspace: its scratch is a fixed array inside the library (4 MiB + 2 KiB on
+ * every GPU that loads it, held until the process exits).  No counterpart in
+ * the reference.
+ *
+ * Arguments and result as tg_int8_gemm_dequant_splitk without the workspace;
+ * TG_ERR_UNSUPPORTED unless M <= 64, N <= 65536 and M * N <= 1048576.
+ * The first call on a device looks up the array's device address (set-up, once
+ * per device); make that first call before any stream capture.  Each call
+ * zeroes the part of the array it uses (a memset on `stream`) before the
+ * kernel.  All calls share the one array, so calls that overlap on the GPU
+ * (different streams, or concurrent host threads) race and corrupt each
+ * other's results: serialise them.
+ */
+int tg_int8_gemm_dequant_splitk_noalloc(const int8_t *xq, const float *xscale, const int8_t *wq,
+                                        const float *wscale, int64_t wscale_numel, const void *bias, int bias_dtype,
+                                        int64_t M, int64_t N, int64_t K, int out_dtype, void *out, void *stream);
+
+/*
  * The tile shape tg_int8_gemm_dequant uses for an M x N problem on the
  * current device: *bn = tile width (UMMA N: 256, 224, 192, 160 or 128) and
  * *pair = 1 when the tile is 256 rows computed by a pair of SMs (tcgen05

@@ -591,3 +591,60 @@ int tg_int8_gemm_dequant_splitk(const int8_t* xq, const float* xscale, const int
 int64_t tg_int8_gemm_dequant_splitk_max_m(void) { return tg::splitk::M_MAX; }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ no-allocation variant
+// The split-K GEMM for callers that must not allocate device memory.  Its
+// scratch is this file-scope array, sized for at most 2^20 accumulator
+// elements (M x N, 4 MiB) and N <= 65536 (2 KiB of tile counters): 4 MiB + 2 KiB
+// that every GPU which loads the library keeps until the process exits.
+namespace {
+
+constexpr int64_t kNoAllocMaxN = 65536;
+constexpr int64_t kNoAllocMaxAcc = int64_t(1) << 20;
+constexpr size_t kNoAllocCountBytes = size_t(kNoAllocMaxN / tg::splitk::BNW) * 4;  // 256-byte multiple
+constexpr size_t kNoAllocBytes = kNoAllocCountBytes + size_t(kNoAllocMaxAcc) * 4;
+
+static __device__ __align__(256) unsigned char g_splitk_scratch[kNoAllocBytes];
+
+// Device address of g_splitk_scratch on `dev` (the current device).  In host
+// code the array's name only stands in for the symbol; its address on a
+// device comes from the runtime, once per device.
+bool noalloc_scratch(int dev, uint8_t** out) {
+  static std::mutex mu;
+  static void* addr[kMaxDevices];
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_splitk_scratch) != cudaSuccess || p == nullptr) return false;
+    addr[dev] = p;
+  }
+  *out = static_cast<uint8_t*>(addr[dev]);
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tg_int8_gemm_dequant_splitk_noalloc(const int8_t* xq, const float* xscale, const int8_t* wq,
+                                        const float* wscale, int64_t wscale_numel, const void* bias, int bias_dtype,
+                                        int64_t M, int64_t N, int64_t K, int out_dtype, void* out, void* stream) {
+  const int chk = check_gemm_args(xq, xscale, wq, wscale, wscale_numel, bias, bias_dtype, M, N, K, out_dtype, out);
+  if (chk != TG_OK || M == 0) return chk;
+  if (M > tg::splitk::M_MAX || N > kNoAllocMaxN || M * N > kNoAllocMaxAcc) return TG_ERR_UNSUPPORTED;
+  int dev;
+  DeviceInfo info;
+  if (!current_device(&dev, &info)) return TG_ERR_CUDA;
+  uint8_t* scratch = nullptr;
+  if (!noalloc_scratch(dev, &scratch)) return TG_ERR_CUDA;
+  // Every call shares the array: zero the counters and this call's part of the
+  // accumulator first, in stream order (a memset, not an allocation).
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(scratch, 0, kNoAllocCountBytes + size_t(M) * size_t(N) * 4, st) != cudaSuccess)
+    return TG_ERR_CUDA;
+  return splitk_launch(xq, xscale, wq, wscale, wscale_numel, bias, bias_dtype, M, N, K, out_dtype, out,
+                       reinterpret_cast<uint32_t*>(scratch), reinterpret_cast<int32_t*>(scratch + kNoAllocCountBytes),
+                       stream);
+}
+
+}  // extern "C"

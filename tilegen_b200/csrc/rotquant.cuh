@@ -260,11 +260,10 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
     // ---- own line (64 values) from the swizzled ring slot ------------------
     float2 vp[32];
     {
-      const uint8_t* lp = buf + line_off;
+      // XOR on the offset (not on a generic pointer) keeps these shared loads.
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        const uint4 w = *reinterpret_cast<const uint4*>(
-            reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(lp) ^ uintptr_t(c << 4)));
+        const uint4 w = *reinterpret_cast<const uint4*>(buf + (line_off ^ uint32_t(c << 4)));
         unpack8<BF16>(w, &vp[4 * c]);
       }
     }

@@ -295,6 +295,79 @@ def _shape_table(dev, flush, stream, iters=20):
     return rows
 
 
+def _quant_sweep(dev, flush, stream, iters=10):
+    """Standalone rotate+quant over group x K x M x dtype (inputs N(0,1), 1 % outlier
+    channels x30): per entry [group, K, M, dtype, us, GB/s, fraction of HBM peak]."""
+    import torch
+
+    from tilegen_b200 import ops
+    from tilegen_b200.synthetic import outlier_activations
+
+    hbm = _peaks()[0]["hbm_gbs"]
+    rows = []
+    for group in (64, 128, 256):
+        if group not in (4, 16, 64, 256):
+            rows.append([group, "unsupported: a ConvRot group is a power of four (H_G = kron of H4)"])
+            continue
+        for k in (1536, 3072, 5120, 13824):
+            for m in (1, 64, 1024, 4096, 65536):
+                for dt in (torch.float16, torch.bfloat16):
+                    x = outlier_activations(m, k, seed=0, dtype=dt, device=dev)
+
+                    def f(e):
+                        e[0].record(stream)
+                        ops.rotate_quant(x, group)
+                        e[1].record(stream)
+
+                    for _ in range(2):
+                        f([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+                    us = statistics.median(r[0] for r in _time_steps(f, iters, flush, stream)) * 1e3
+                    gbs = (m * k * 3 + 4 * m) / (us * 1e-6) / 1e9
+                    rows.append([group, k, m, "fp16" if dt == torch.float16 else "bf16", round(us, 2),
+                                 round(gbs, 1), round(gbs / hbm, 4)])
+                    del x
+    return rows
+
+
+def _dit_block_bf16(dev, flush, stream, world, rank, tokens=65520, iters=10):
+    """The DiT projection set on bf16 activations, `tokens` rows sharded over the ranks:
+    per shape the max-over-ranks int8 linear and bf16 cuBLAS times and aggregate tokens/s."""
+    import torch
+    import torch.distributed as dist
+
+    from tilegen_b200 import ops
+    from tilegen_b200.sharding import shard_bounds
+    from tilegen_b200.synthetic import DIT_SHAPES, dit_activations, gaussian_weight
+
+    lo, hi = shard_bounds(tokens, world, rank)
+    m = hi - lo
+    rows = []
+    for name, k, n in DIT_SHAPES:
+        x = dit_activations(name, m, seed=rank, dtype=torch.bfloat16, device=dev)
+        w = gaussian_weight(n, k, seed=1, dtype=torch.bfloat16, device=dev)
+        wq, ws = ops.rotate_quant(w, GROUP)
+
+        def lin(e):
+            e[0].record(stream)
+            xq, xs = ops.rotate_quant(x, GROUP)
+            ops.int8_gemm_dequant(xq, xs, wq, ws, None, torch.bfloat16)
+            e[1].record(stream)
+
+        for _ in range(2):
+            lin([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+        tl = statistics.mean(r[0] for r in _time_steps(lin, iters, flush, stream)) * 1e3
+        tb = _bf16_linear_us(x, w, iters, flush, stream)
+        t = torch.tensor([tl, tb], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tl, tb = float(t[0]), float(t[1])
+        rows.append({"shape": name, "K": k, "N": n, "rows_per_gpu": m, "int8_linear_us": round(tl, 1),
+                     "bf16_cublas_us": round(tb, 1), "speedup_vs_bf16": round(tb / tl, 3),
+                     "tokens_per_s": round(tokens / (tl * 1e-6), 1)})
+        del x, w, wq, ws
+    return rows
+
+
 def run_tilegen(args):
     import torch
     import torch.distributed as dist
@@ -393,9 +466,13 @@ def run_tilegen(args):
     int8_lib_tops = _int_mm_tops(dev)
     status = _lib.device_status(local)
 
-    shapes = cpu = None
+    shapes = cpu = sweep = None
+    if world > 1:
+        dist.barrier()
+    block = _dit_block_bf16(dev, flush, stream, world, rank)
     if world == 1:
         shapes = _shape_table(dev, flush, stream)
+        sweep = _quant_sweep(dev, flush, stream)
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu_us, cores, sample = _cpu_baseline_us(k, n)
         cpu = {"value": round(cpu_us, 1), "unit": "us", "cores": cores, "kind": "port", "sample": sample}
@@ -451,6 +528,9 @@ def run_tilegen(args):
         line["cpu_baseline"] = cpu
     if shapes is not None:
         line["dit_shapes"] = shapes
+    line["dit_block_bf16"] = {"tokens": 65520, "rows_sharded_over": world, "shapes": block}
+    if sweep is not None:
+        line["quant_sweep"] = {"columns": ["group", "K", "M", "dtype", "us", "GB/s", "frac_of_hbm"], "rows": sweep}
     print(json.dumps(line), flush=True)
 
 

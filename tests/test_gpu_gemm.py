@@ -149,3 +149,20 @@ def test_custom_op_and_status(cuda):
     b = ops.int8_gemm_dequant(xq.to(cuda), xs.to(cuda), wq.to(cuda), ws.to(cuda), bias.to(cuda), torch.float16)
     assert torch.equal(a, b)
     assert _lib.device_status(0) == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(9000, 1000, 1024), (65520, 512, 256)])
+def test_large_m_spans_several_tile_groups(cuda, m, n, k):
+    # More than 16 pair m-tiles: the tile order walks groups of 16 m-tiles; every
+    # tile must still be computed once.  Exact reference: int8 products summed in
+    # float64 (|sum| < 2^53), one rounding to fp32, then the fp32 epilogue.
+    g = torch.Generator().manual_seed(m + n)
+    xq = torch.randint(-128, 128, (m, k), generator=g, dtype=torch.int8).to(cuda)
+    wq = torch.randint(-128, 128, (n, k), generator=g, dtype=torch.int8).to(cuda)
+    xs = (torch.rand(m, generator=g) * 0.02 + 1e-4).to(cuda)
+    ws = (torch.rand(n, generator=g) * 0.01 + 1e-5).to(cuda)
+    y = ops.int8_gemm_dequant(xq, xs, wq, ws, None, torch.float16)
+    acc = (xq.double() @ wq.double().t()).float()
+    ref = (acc * xs[:, None] * ws[None, :]).to(torch.float16)
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))

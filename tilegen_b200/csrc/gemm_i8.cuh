@@ -26,7 +26,8 @@
 //   Both CTAs' loads complete on the even CTA's ring barriers; its MMA thread
 //   issues for the pair and its commits arrive on both CTAs' barriers; both
 //   epilogues release an accumulator by arriving on the even CTA's barrier.
-// Tiles are walked M-fastest so the CTAs in flight share weight columns in L2.
+// Tiles are walked M-fastest within groups of 16 m-tiles (tile_coords), so the
+// CTAs in flight share weight columns in L2 and A stays in L2 across a group.
 // Every mbarrier wait is bounded (see common.cuh); a role that gives up stops
 // the others in its CTA, and the peer CTA's waits then expire as well.
 #pragma once
@@ -90,6 +91,24 @@ struct GemmParams {
   int m_tiles, n_tiles, k_blocks;  // m_tiles: 128-row (single) or 256-row (pair) tiles;
                                    // k_blocks: ring slots of ksub(pair) * 128 bytes of K
 };
+
+// m-tiles per group of the tile order: 16 (4096 rows of A in pair tiles) keeps
+// a group's A in L2 while its column tiles stream past.
+constexpr int kTileGroupM = 16;
+
+// Tile t -> (m-tile, n-tile).  Groups of kTileGroupM m-tiles, one after the
+// other; inside a group tiles go M-fastest, so the CTAs in flight share weight
+// columns in L2 and A is read from HBM about once (a plain M-fastest order
+// over a large M would read all of A again for every column tile).
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& mt, int& nt) {
+  const int per_group = kTileGroupM * p.n_tiles;
+  const int group = t / per_group;
+  const int first = group * kTileGroupM;
+  const int size = min(kTileGroupM, p.m_tiles - first);
+  const int r = t - group * per_group;
+  mt = first + r % size;
+  nt = r / size;
+}
 
 // BN: tile width (a multiple of 32, at most 256); OUT: 0 fp32, 1 fp16, 2 bf16
 // (tg_dtype codes); PAIR: see above (launched with clusters of 2 CTAs).
@@ -194,8 +213,10 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int t = unit; t < num_tiles; t += units) {
-        const int m0 = (t % p.m_tiles) * TILE_M + int(rank) * BM;
-        const int n0 = (t / p.m_tiles) * BN + int(rank) * BROWS;
+        int mt, nt;
+        tile_coords(t, p, mt, nt);
+        const int m0 = mt * TILE_M + int(rank) * BM;
+        const int n0 = nt * BN + int(rank) * BROWS;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!wait(&empty_bar[stage], phase ^ 1u, DEVERR_PIPE_TIMEOUT)) goto done;
           if (PAIR) {
@@ -271,8 +292,10 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     const uint32_t tempty_leader1 = PAIR ? mapa_shared(smem_u32(&tempty_bar[1]), 0) : 0u;
     int local = 0;
     for (int t = unit; t < num_tiles; t += units, ++local) {
-      const int m0 = (t % p.m_tiles) * TILE_M + int(rank) * BM;
-      const int n0 = (t / p.m_tiles) * BN;
+      int mt, nt;
+      tile_coords(t, p, mt, nt);
+      const int m0 = mt * TILE_M + int(rank) * BM;
+      const int n0 = nt * BN;
       const int ab = local & 1;
       // Column parameters of this tile (shared by the four epilogue warps).
       named_barrier(1, 128);

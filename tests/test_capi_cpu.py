@@ -66,3 +66,34 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "nope.so"))
     with pytest.raises(RuntimeError, match="missing"):
         _lib.lib()
+
+
+def test_small_m_entry_points_check_before_device_work():
+    L = _lib.lib()
+    p = ctypes.c_void_p(256)
+    L.tg_int8_gemm_dequant_splitk_noalloc.argtypes = [ctypes.c_void_p] * 4 + [
+        ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    assert L.tg_int8_gemm_dequant_splitk_max_m() == 64
+    # workspace: 128-column tile counters (256-byte rounded), then M x N int32
+    assert L.tg_int8_gemm_dequant_splitk_workspace(1, 128) == 256 + 512
+    assert L.tg_int8_gemm_dequant_splitk_workspace(64, 15360) == 512 + 64 * 15360 * 4
+    assert L.tg_int8_gemm_dequant_splitk_workspace(-1, 128) == 0
+    big = 1 << 30
+    # M above the limit, workspace missing, too small or misaligned
+    assert L.tg_int8_gemm_dequant_splitk(p, p, p, p, 1, None, 0, 65, 128, 64, 1, p, p, big, None) == \
+        _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_int8_gemm_dequant_splitk(p, p, p, p, 1, None, 0, 8, 128, 64, 1, p, None, big, None) == \
+        _lib.TG_ERR_INVALID_ARG
+    assert L.tg_int8_gemm_dequant_splitk(p, p, p, p, 1, None, 0, 8, 128, 64, 1, p, p, 16, None) == \
+        _lib.TG_ERR_INVALID_ARG
+    assert L.tg_int8_gemm_dequant_splitk(p, p, p, p, 1, None, 0, 8, 128, 64, 1, p, ctypes.c_void_p(272), big,
+                                         None) == _lib.TG_ERR_MISALIGNED
+    assert L.tg_int8_gemm_dequant_splitk(None, None, None, None, 1, None, 0, 0, 128, 64, 1, None, None, 0,
+                                         None) == _lib.TG_OK
+    # the no-allocation variant: its array's limits
+    for m, n in ((65, 128), (64, 32768), (8, 65536 + 128)):
+        assert L.tg_int8_gemm_dequant_splitk_noalloc(p, p, p, p, 1, None, 0, m, n, 64, 1, p, None) == \
+            _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_int8_gemm_dequant_splitk_noalloc(None, None, None, None, 1, None, 0, 0, 128, 64, 1, None,
+                                                 None) == _lib.TG_OK

@@ -4,9 +4,10 @@
  * Plain pointers and sizes only.  Every compute entry point
  *   - takes device pointers and a cudaStream_t passed as `void *stream`
  *     (NULL = the legacy default stream) and only enqueues work on it: no host
- *     synchronisation, no allocation (callers own every buffer, so the calls
- *     can be captured in CUDA graphs);
+ *     synchronisation, no allocation;
  *   - returns a tg_status; nothing is launched when it is not TG_OK.
+ * tg_rotate_quant, tg_int8_gemm_dequant and tg_int8_gemm_dequant_splitk work
+ * only on buffers the caller owns, so they can be captured in CUDA graphs.
  * Device-side failures (a bounded wait that gave up) are recorded in a device
  * status word that tg_device_status() reads.
  *

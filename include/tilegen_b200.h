@@ -17,6 +17,7 @@
 #ifndef TILEGEN_B200_H
 #define TILEGEN_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus

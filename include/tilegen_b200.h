@@ -87,14 +87,14 @@ int tg_int8_gemm_dequant(const int8_t *xq, const float *xscale, const int8_t *wq
                          int64_t K, int out_dtype, void *out, void *stream);
 
 /*
- * The same GEMM + dequantisation for few activation rows (1 <= M <= 64, decode
+ * The same GEMM + dequantisation for few activation rows (1 <= M <= 128, decode
  * and preview steps), bit-identical to tg_int8_gemm_dequant.  Also replaces
  * `int8_matmul_dequant_chunked` (tilegen/quant/int8_ops.py:22-70), whose GEMM
  * at small M is whatever torch._int_mm does.  The weight streams through all
  * SMs: K is split across CTAs, each adds its exact int32 partial sums into a
  * scratch accumulator, and the last CTA of each 128-column tile dequantises.
  *
- * Arguments as tg_int8_gemm_dequant (M > 64 gives TG_ERR_UNSUPPORTED), plus:
+ * Arguments as tg_int8_gemm_dequant (M > 128 gives TG_ERR_UNSUPPORTED), plus:
  *   workspace  tg_int8_gemm_dequant_splitk_workspace(M, N) bytes, 256-byte
  *              aligned, ZERO-FILLED before its first use; every call leaves it
  *              zero again (also one whose wait expired), so it needs no
@@ -109,7 +109,7 @@ int tg_int8_gemm_dequant_splitk(const int8_t *xq, const float *xscale, const int
 /* Workspace bytes tg_int8_gemm_dequant_splitk needs for an M x N output. */
 size_t tg_int8_gemm_dequant_splitk_workspace(int64_t M, int64_t N);
 
-/* Largest M tg_int8_gemm_dequant_splitk accepts (64). */
+/* Largest M tg_int8_gemm_dequant_splitk accepts (128). */
 int64_t tg_int8_gemm_dequant_splitk_max_m(void);
 
 /*

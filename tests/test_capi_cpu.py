@@ -74,14 +74,14 @@ def test_small_m_entry_points_check_before_device_work():
     L.tg_int8_gemm_dequant_splitk_noalloc.argtypes = [ctypes.c_void_p] * 4 + [
         ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
-    assert L.tg_int8_gemm_dequant_splitk_max_m() == 64
+    assert L.tg_int8_gemm_dequant_splitk_max_m() == 128
     # workspace: 128-column tile counters (256-byte rounded), then M x N int32
     assert L.tg_int8_gemm_dequant_splitk_workspace(1, 128) == 256 + 512
     assert L.tg_int8_gemm_dequant_splitk_workspace(64, 15360) == 512 + 64 * 15360 * 4
     assert L.tg_int8_gemm_dequant_splitk_workspace(-1, 128) == 0
     big = 1 << 30
     # M above the limit, workspace missing, too small or misaligned
-    assert L.tg_int8_gemm_dequant_splitk(p, p, p, p, 1, None, 0, 65, 128, 64, 1, p, p, big, None) == \
+    assert L.tg_int8_gemm_dequant_splitk(p, p, p, p, 1, None, 0, 129, 128, 64, 1, p, p, big, None) == \
         _lib.TG_ERR_UNSUPPORTED
     assert L.tg_int8_gemm_dequant_splitk(p, p, p, p, 1, None, 0, 8, 128, 64, 1, p, None, big, None) == \
         _lib.TG_ERR_INVALID_ARG

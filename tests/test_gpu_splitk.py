@@ -1,11 +1,11 @@
 """Parity of the small-M split-K INT8 GEMM (tg_int8_gemm_dequant_splitk) on the GPU.
 
-With M <= 64 rows the weight is streamed by (N/128 column tiles) x (K slices)
+With M <= 128 rows the weight is streamed by (N/128 column tiles) x (K slices)
 CTAs whose exact int32 partial sums meet in a scratch accumulator; the last
 slice of a tile dequantises.  Integer addition makes the sums order-independent,
 so the output must be bit-identical to the tiled kernel, to the oracle, and to
 the reference's torch sequence (tilegen/quant/int8_ops.py:22-70, torch._int_mm
-is exact), for every M from 1 to 64, ragged N and K, all output dtypes, bias
+is exact), for every M from 1 to 128, ragged N and K, all output dtypes, bias
 and scale variants, and repeated calls on one scratch.
 """
 from __future__ import annotations
@@ -37,15 +37,16 @@ def _bits(y):
 
 
 def _run(case, out_dtype, dev, max_m):
+    """int8_gemm_dequant with every M <= max_m on the split-K kernel (0: the tiled kernel)."""
     xq, xs, wq, ws, bias = case
-    old = ops.SPLITK_MAX_M
-    ops.SPLITK_MAX_M = max_m
+    route = ops.splitk_route
+    ops.splitk_route = lambda m, n, k: 0 < m <= max_m
     try:
         y = ops.int8_gemm_dequant(xq.to(dev), xs.to(dev), wq.to(dev), ws.to(dev),
                                   None if bias is None else bias.to(dev), out_dtype)
         torch.cuda.synchronize()
     finally:
-        ops.SPLITK_MAX_M = old
+        ops.splitk_route = route
     return y
 
 
@@ -55,10 +56,10 @@ def _healthy_device(cuda):
     assert _lib.device_status(0) == 0, "a bounded wait expired during the test"
 
 
-@pytest.mark.parametrize("m", [1, 2, 7, 16, 17, 31, 32, 33, 48, 63, 64])
+@pytest.mark.parametrize("m", [1, 2, 7, 16, 17, 31, 32, 33, 48, 63, 64, 65, 96, 100, 127, 128])
 def test_rows_bit_exact_vs_tiled_kernel(cuda, m):
-    case = _case(m, 1536, 8192, seed=m)  # K >= 8192: split-K for every M <= 64
-    a = _run(case, torch.float16, cuda, 64)
+    case = _case(m, 1536, 2048, seed=m)
+    a = _run(case, torch.float16, cuda, 128)
     b = _run(case, torch.float16, cuda, 0)
     assert np.array_equal(_bits(a), _bits(b))
 
@@ -69,7 +70,7 @@ def test_rows_bit_exact_vs_tiled_kernel(cuda, m):
 def test_against_oracle(cuda, out_dtype, bias_dtype, scalar_ws):
     m, n, k = 24, 640, 1152
     case = _case(m, n, k, seed=3, scalar_ws=scalar_ws, bias_dtype=bias_dtype)
-    y = _run(case, out_dtype, cuda, 64)
+    y = _run(case, out_dtype, cuda, 128)
     xq, xs, wq, ws, bias = case
     ref = oracle.int8_gemm_dequant(xq.numpy(), xs.numpy(), wq.numpy(), ws.numpy(),
                                    None if bias is None else bias.float().numpy(), DT_NAME[out_dtype])
@@ -82,9 +83,9 @@ def test_against_oracle(cuda, out_dtype, bias_dtype, scalar_ws):
 
 @pytest.mark.parametrize("n,k", [(8, 16), (136, 144), (1000, 4112), (5120, 13824), (15360, 5120)])
 def test_ragged_and_dit_shapes(cuda, n, k):
-    for m in (1, 64):
+    for m in (1, 64, 128):
         case = _case(m, n, k, seed=n + k + m)
-        a = _run(case, torch.bfloat16, cuda, 64)
+        a = _run(case, torch.bfloat16, cuda, 128)
         xq, xs, wq, ws, _ = case
         # int8 products summed in float64 are exact (|sum| < 2^53); .float()
         # then rounds once, as float(int32) does.
@@ -97,7 +98,7 @@ def test_scratch_is_left_zero_and_reused(cuda):
     outs, refs = [], []
     for i in range(5):
         case = _case(40, 2048, 3072, seed=100 + i, bias_dtype=torch.float32)
-        outs.append(_run(case, torch.float16, cuda, 64))
+        outs.append(_run(case, torch.float16, cuda, 128))
         refs.append(_run(case, torch.float16, cuda, 0))
     for a, b in zip(outs, refs):
         assert np.array_equal(_bits(a), _bits(b))

@@ -521,7 +521,7 @@ int splitk_launch(const int8_t* xq, const float* xscale, const int8_t* wq, const
   int dev;
   DeviceInfo info;
   if (!current_device(&dev, &info)) return TG_ERR_CUDA;
-  const int mpad = int((M + 15) / 16 * 16);
+  const int mpad = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
   const int tiles = int((N + BNW - 1) / BNW);
   const int k_blocks = int((K + BK - 1) / BK);
   // About 1.6 CTAs per SM stream the weight (measured at M=1 on the DiT
@@ -559,8 +559,8 @@ int splitk_launch(const int8_t* xq, const float* xscale, const int8_t* wq, const
   switch (mpad) {
     case 16: return launch_splitk_m<16>(tw, tx, p, tiles, out_dtype, hb, dev, st);
     case 32: return launch_splitk_m<32>(tw, tx, p, tiles, out_dtype, hb, dev, st);
-    case 48: return launch_splitk_m<48>(tw, tx, p, tiles, out_dtype, hb, dev, st);
-    default: return launch_splitk_m<64>(tw, tx, p, tiles, out_dtype, hb, dev, st);
+    case 64: return launch_splitk_m<64>(tw, tx, p, tiles, out_dtype, hb, dev, st);
+    default: return launch_splitk_m<128>(tw, tx, p, tiles, out_dtype, hb, dev, st);
   }
 }
 
@@ -600,6 +600,7 @@ int64_t tg_int8_gemm_dequant_splitk_max_m(void) { return tg::splitk::M_MAX; }
 // that every GPU which loads the library keeps until the process exits.
 namespace {
 
+constexpr int64_t kNoAllocMaxM = 64;
 constexpr int64_t kNoAllocMaxN = 65536;
 constexpr int64_t kNoAllocMaxAcc = int64_t(1) << 20;
 constexpr size_t kNoAllocCountBytes = size_t(kNoAllocMaxN / tg::splitk::BNW) * 4;  // 256-byte multiple
@@ -632,7 +633,7 @@ int tg_int8_gemm_dequant_splitk_noalloc(const int8_t* xq, const float* xscale, c
                                         int64_t M, int64_t N, int64_t K, int out_dtype, void* out, void* stream) {
   const int chk = check_gemm_args(xq, xscale, wq, wscale, wscale_numel, bias, bias_dtype, M, N, K, out_dtype, out);
   if (chk != TG_OK || M == 0) return chk;
-  if (M > tg::splitk::M_MAX || N > kNoAllocMaxN || M * N > kNoAllocMaxAcc) return TG_ERR_UNSUPPORTED;
+  if (M > kNoAllocMaxM || N > kNoAllocMaxN || M * N > kNoAllocMaxAcc) return TG_ERR_UNSUPPORTED;
   int dev;
   DeviceInfo info;
   if (!current_device(&dev, &info)) return TG_ERR_CUDA;

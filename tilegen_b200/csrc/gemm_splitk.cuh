@@ -1,4 +1,4 @@
-// Small-M INT8 GEMM with the dequantising epilogue (sm_100a), for M <= 64
+// Small-M INT8 GEMM with the dequantising epilogue (sm_100a), for M <= 128
 // activation rows (decode / preview steps):
 //
 //   out[m,n] = ((float(sum_k xq[m,k]*wq[n,k]) * xscale[m]) * wscale[n]) + bias[n]
@@ -8,7 +8,7 @@
 // tiles of gemm_i8.cuh would put only N/256 CTAs on that stream.  Here:
 //  * The roles of the operands are swapped: a 128-row tile of the WEIGHT is
 //    the UMMA M operand and the (zero-padded) activation rows are UMMA N
-//    (MPAD = 16..64), so D[n, m] accumulates in a 128-lane x MPAD-column
+//    (MPAD = 16, 32, 64 or 128), so D[n, m] accumulates in a 128-lane x MPAD-column
 //    TMEM tile (tcgen05 kind::i8, int32).
 //  * K is split: CTA (s, t) multiplies column tile t over k-blocks
 //    [s*kb_per_slice, ...), so that N/128 x slices CTAs stream the weight
@@ -35,11 +35,12 @@ constexpr int BK = 128;                  // bytes of K per k-block
 constexpr int UK = 32;                   // K per tcgen05.mma kind::i8
 constexpr uint32_t W_BYTES = BNW * BK;   // 16 KB
 constexpr int THREADS = 192;
-constexpr int M_MAX = 64;
-constexpr int STAGES = 4;
+constexpr int M_MAX = 128;
+// Ring depth: 4 slots, 3 when the activation tile is 128 rows (two CTAs per SM).
+__host__ __device__ constexpr int stages(int mpad) { return mpad <= 64 ? 4 : 3; }
 __host__ __device__ constexpr uint32_t x_bytes(int mpad) { return uint32_t(mpad) * BK; }
 __host__ __device__ constexpr uint32_t stage_bytes(int mpad) { return W_BYTES + x_bytes(mpad); }
-__host__ __device__ constexpr uint32_t smem_bytes(int mpad) { return STAGES * stage_bytes(mpad) + 1024; }
+__host__ __device__ constexpr uint32_t smem_bytes(int mpad) { return stages(mpad) * stage_bytes(mpad) + 1024; }
 }  // namespace splitk
 
 struct SplitKParams {
@@ -57,7 +58,7 @@ struct SplitKParams {
   void* out;         // [M, N] of OUT
 };
 
-// MPAD: activation rows padded to a multiple of 16 (the UMMA N); OUT: tg_dtype.
+// MPAD: activation rows padded to 16, 32, 64 or 128 (the UMMA N); OUT: tg_dtype.
 template <int MPAD, int OUT, bool HAS_BIAS>
 __global__ void __launch_bounds__(splitk::THREADS, 1)
     gemm_i8_splitk_kernel(const __grid_constant__ CUtensorMap tma_w, const __grid_constant__ CUtensorMap tma_x,
@@ -66,7 +67,8 @@ __global__ void __launch_bounds__(splitk::THREADS, 1)
   static_assert(MPAD % 16 == 0 && MPAD >= 16 && MPAD <= M_MAX, "padded rows");
   constexpr uint32_t XB = x_bytes(MPAD);
   constexpr uint32_t TX_BYTES = W_BYTES + XB;
-  constexpr uint32_t TMEM_COLS = MPAD <= 32 ? 32 : 64;
+  constexpr int STAGES = stages(MPAD);
+  constexpr uint32_t TMEM_COLS = MPAD <= 32 ? 32 : (MPAD <= 64 ? 64 : 128);
   constexpr uint32_t IDESC = gemm::idesc(BNW, MPAD);
 
   extern __shared__ uint8_t smem_raw[];
@@ -184,18 +186,21 @@ __global__ void __launch_bounds__(splitk::THREADS, 1)
     const bool got = __all_sync(0xffffffffu, wait(&tfull_bar, 0u, DEVERR_MMA_TIMEOUT));
     if (got) {
       tc_fence_after();
-      uint32_t v[MPAD];
+      // 16 columns (activation rows) at a time; coalesced over the warp: 32
+      // consecutive n of one row m per add.
+      int32_t* a = p.acc + n;
+      const size_t stride = size_t(p.N);
+#pragma unroll 1
+      for (int h = 0; h < MPAD; h += 16) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(h), v);
+        tmem_wait_ld();
+        if (n < p.N) {
 #pragma unroll
-      for (int h = 0; h < MPAD / 16; ++h)
-        tmem_ld_32x32b_x16(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(h * 16),
-                           *reinterpret_cast<uint32_t(*)[16]>(&v[h * 16]));
-      tmem_wait_ld();
-      // Coalesced over the warp: 32 consecutive n of one row m per step.
-      if (n < p.N) {
-        int32_t* a = p.acc + n;
-#pragma unroll
-        for (int m = 0; m < MPAD; ++m)
-          if (m < p.M) atomicAdd(a + size_t(m) * p.N, static_cast<int32_t>(v[m]));
+          for (int j = 0; j < 16; ++j)
+            if (h + j < p.M) atomicAdd(a + j * stride, static_cast<int32_t>(v[j]));
+        }
+        a += 16 * stride;
       }
       __threadfence();
     }
@@ -217,34 +222,39 @@ __global__ void __launch_bounds__(splitk::THREADS, 1)
           else if (p.bias_dtype == TG_DT_F16) bs = __half2float(static_cast<const __half*>(p.bias)[n]);
           else bs = __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n]);
         }
-        // Rows are finished 16 at a time: their sums are all loaded before any
+        // Rows are finished 32 at a time: their sums are all loaded before any
         // is used, so the L2 latencies overlap instead of adding up.
         const size_t stride = size_t(p.N);
         int32_t* arow = p.acc + n;
         char* orow = static_cast<char*>(p.out) + size_t(n) * (OUT == 0 ? 4 : 2);
         const size_t ostride = stride * (OUT == 0 ? 4 : 2);
+        constexpr int RB = MPAD < 32 ? MPAD : 32;
+#pragma unroll 1
+        for (int m0 = 0; m0 < MPAD; m0 += RB) {
+          int32_t a[RB];
+          {
+            const int32_t* ap = arow;
 #pragma unroll
-        for (int m0 = 0; m0 < MPAD; m0 += 16) {
-          int32_t a[16];
+            for (int j = 0; j < RB; ++j, ap += stride)
+              if (m0 + j < p.M) a[j] = __ldcg(ap);
+          }
+          int32_t* zp = arow;
+          char* o = orow;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (m0 + j < p.M) a[j] = __ldcg(arow + j * stride);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
+          for (int j = 0; j < RB; ++j, zp += stride, o += ostride) {
             if (m0 + j < p.M) {
-              __stcg(arow + j * stride, 0);
+              __stcg(zp, 0);
               float r = __int2float_rn(a[j]);
               r = __fmul_rn(r, __ldg(p.xscale + m0 + j));
               r = __fmul_rn(r, ws);
               if (HAS_BIAS) r = __fadd_rn(r, bs);
-              char* o = orow + j * ostride;
               if (OUT == 0) *reinterpret_cast<float*>(o) = r;
               else if (OUT == 1) *reinterpret_cast<__half*>(o) = __float2half_rn(r);
               else *reinterpret_cast<__nv_bfloat16*>(o) = __float2bfloat16_rn(r);
             }
           }
-          arow += 16 * stride;
-          orow += 16 * ostride;
+          arow += RB * stride;
+          orow += RB * ostride;
         }
       }
       named_barrier(1, 128);

@@ -112,7 +112,7 @@ def int8_gemm_dequant(xq: torch.Tensor, xscale: torch.Tensor, wq: torch.Tensor, 
         bias = b
         b_ptr, b_code = b.data_ptr(), _DTYPE_CODE[b.dtype]
     out = torch.empty((m, n), dtype=out_dtype, device=dev)
-    if 0 < m <= SPLITK_MAX_M and (m <= 16 or k >= 8192):
+    if m and splitk_route(m, n, k):
         work = _splitk_workspace(dev, m, n)
         _call("tg_int8_gemm_dequant_splitk", dev, xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),
               ws.numel(), b_ptr, b_code, m, n, k, _DTYPE_CODE[out_dtype], out.data_ptr(), work.data_ptr(),
@@ -123,11 +123,21 @@ def int8_gemm_dequant(xq: torch.Tensor, xscale: torch.Tensor, wq: torch.Tensor, 
     return out
 
 
-# int8_gemm_dequant takes the split-K kernel (tg_int8_gemm_dequant_splitk) for
-# M <= 16, and up to SPLITK_MAX_M rows when K >= 8192: measured on B200 at the
-# DiT shapes, the tiled kernel is faster from M ~ 32 unless K is long.
-# 0 sends every M to the tiled kernel.
-SPLITK_MAX_M = 64
+# Largest M int8_gemm_dequant sends to the split-K kernel
+# (tg_int8_gemm_dequant_splitk); 0 sends every M to the tiled kernel.
+SPLITK_MAX_M = 128
+
+
+def splitk_route(m: int, n: int, k: int) -> bool:
+    """Whether an m x n x k product goes to the split-K kernel (at most SPLITK_MAX_M rows).
+
+    Measured on B200 at the DiT shapes against the tiled kernel (whose M <= 128
+    tiles give only N/128 CTAs): split-K is faster for M <= 16 everywhere, up to
+    64 rows when N <= 8192, and up to 128 rows when K >= 8192.
+    """
+    if not 0 < m <= SPLITK_MAX_M:
+        return False
+    return m <= 16 or (m <= 64 and n <= 8192) or (m <= 128 and k >= 8192)
 
 # Split-K scratch, one per (device, stream): zero-filled when created and left
 # zero by every call, so it is reused as is; it only grows.

@@ -6,8 +6,9 @@
  *     (NULL = the legacy default stream) and only enqueues work on it: no host
  *     synchronisation, no allocation;
  *   - returns a tg_status; nothing is launched when it is not TG_OK.
- * tg_rotate_quant, tg_int8_gemm_dequant and tg_int8_gemm_dequant_splitk work
- * only on buffers the caller owns, so they can be captured in CUDA graphs.
+ * tg_rotate_quant, tg_quantize_act, tg_int8_gemm_dequant and
+ * tg_int8_gemm_dequant_splitk work only on buffers the caller owns, so they
+ * can be captured in CUDA graphs.
  * Device-side failures (a bounded wait that gave up) are recorded in a device
  * status word that tg_device_status() reads.
  *
@@ -34,6 +35,10 @@ typedef enum {
 } tg_status;
 
 typedef enum { TG_DT_F32 = 0, TG_DT_F16 = 1, TG_DT_BF16 = 2 } tg_dtype;
+
+/* Input activations tg_quantize_act applies before quantising (the names of
+ * the reference's `input_act`, tilegen/comfyui/backend.py:174,201-204). */
+typedef enum { TG_ACT_NONE = 0, TG_ACT_GELU_TANH = 1, TG_ACT_GELU = 2 } tg_act;
 
 /* Library version, (major << 16) | minor. */
 int tg_version(void);
@@ -62,8 +67,32 @@ const char *tg_status_string(int status);
 int tg_rotate_quant(const void *x, int x_dtype, int64_t M, int64_t K, int group, int8_t *q, float *scale,
                     void *stream);
 
-/* Largest K tg_rotate_quant accepts (a multiple of 256). */
+/* Largest K tg_rotate_quant and tg_quantize_act accept (a multiple of 256). */
 int64_t tg_rotate_quant_max_k(void);
+
+/*
+ * tg_rotate_quant with the production wrapper's two other options fused into
+ * the same pass over x (tilegen/comfyui/backend.py:166-244):
+ *
+ *   act    TG_ACT_NONE, TG_ACT_GELU_TANH or TG_ACT_GELU: the input activation
+ *          of backend.py:201-204, applied first.  Evaluated in fp32 as torch's
+ *          CUDA GELU kernels do (gelu_tanh: 0.5x(1+tanh(sqrt(2/pi)(x+0.044715x^3))),
+ *          gelu: 0.5x(1+erf(x/sqrt(2)))) and rounded to x_dtype, exactly what
+ *          the separate activation op would have stored for the quantiser.
+ *   group  4, 16, 64 or 256: as tg_rotate_quant on act(x) (K % 256 == 0);
+ *          1: no rotation, the row-wise branch of backend.py:230-232 (K % 64 == 0):
+ *            scale[m] = max(absmax_m * fp32(1/127), 1e-30)   (NaN propagates)
+ *            q[m,k]   = int8(clamp(rint(dtype(y[m,k] / dtype(scale[m]))), -128, 127))
+ *          with y = act(x), the division in IEEE fp32, dtype() rounding to
+ *          x_dtype, and NaN codes (0/0 when dtype(scale) underflows to 0 in
+ *          fp16) stored as 0 -- torch's evaluation of those two lines on CUDA.
+ *
+ * tg_quantize_act(x, dt, M, K, G, TG_ACT_NONE, q, scale, s) runs the same
+ * kernel as tg_rotate_quant(x, dt, M, K, G, q, scale, s) for G > 1.
+ * TG_ERR_INVALID_ARG for an unknown act.  M == 0 is a no-op.
+ */
+int tg_quantize_act(const void *x, int x_dtype, int64_t M, int64_t K, int group, int act, int8_t *q, float *scale,
+                    void *stream);
 
 /*
  * INT8 GEMM with the dequantisation fused into the epilogue (tcgen05 kind::i8,

@@ -3,8 +3,9 @@
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg
 use this package, and only as the checker / the timed CPU baseline.  It wraps
 ``liboracle.so`` (``convrot_oracle.c``, a plain-C restatement of
-tilegen/kernels/int8_convrot.py:47-104 and tilegen/quant/int8_ops.py:22-70;
-see that file's header for the per-step citations).
+tilegen/kernels/int8_convrot.py:47-104, tilegen/quant/int8_ops.py:22-70 and
+tilegen/comfyui/backend.py:230-232; see that file's header for the per-step
+citations).
 
 Parity is pinned: ``tests/test_oracle.py`` checks this oracle against the
 fixtures in ``tests/golden/``, which the reference's own eager functions
@@ -44,6 +45,8 @@ def lib() -> ctypes.CDLL:
         i64, p = ctypes.c_int64, ctypes.c_void_p
         L.oracle_rotate_quant.argtypes = [p, ctypes.c_int, i64, i64, ctypes.c_int, p, p]
         L.oracle_rotate_quant.restype = ctypes.c_int
+        L.oracle_rowwise_quant.argtypes = [p, ctypes.c_int, i64, i64, p, p]
+        L.oracle_rowwise_quant.restype = ctypes.c_int
         L.oracle_int8_gemm_dequant.argtypes = [p, p, p, p, i64, p, i64, i64, i64, ctypes.c_int, p]
         L.oracle_int8_gemm_dequant.restype = ctypes.c_int
         L.oracle_num_threads.restype = ctypes.c_int
@@ -69,6 +72,18 @@ def rotate_quant(x: np.ndarray, dtype: str, group: int = 256):
     rc = lib().oracle_rotate_quant(_ptr(x), _DTYPE_CODES[dtype], m, k, group, _ptr(q), _ptr(s))
     if rc != 0:
         raise ValueError(f"oracle_rotate_quant rejected M={m} K={k} group={group}")
+    return q, s
+
+
+def rowwise_quant(x: np.ndarray, dtype: str):
+    """Rotation-free row-wise int8 of ``x`` (raw fp16/bf16 patterns) -> ``(q, scale)``."""
+    x = np.ascontiguousarray(x)
+    m, k = x.shape
+    q = np.empty((m, k), np.int8)
+    s = np.empty((m,), np.float32)
+    rc = lib().oracle_rowwise_quant(_ptr(x), _DTYPE_CODES[dtype], m, k, _ptr(q), _ptr(s))
+    if rc != 0:
+        raise ValueError(f"oracle_rowwise_quant rejected M={m} K={k} dtype={dtype}")
     return q, s
 
 

@@ -3,7 +3,7 @@
  * checker that the CUDA kernels are compared against, and the CPU baseline that
  * bench.py times.  The product path never calls it.
  *
- * Two functions, each a plain-C restatement of the reference's algorithm:
+ * Three functions, each a plain-C restatement of the reference's algorithm:
  *
  *  oracle_rotate_quant  - tilegen/kernels/int8_convrot.py:47-104 (`fht_quant`):
  *      per 256-wide group, four radix-4 butterfly stages on the (non-Sylvester)
@@ -21,6 +21,15 @@
  *      out = ((float(acc) * xscale[m]) * wscale[n]) + bias[n] in fp32, one
  *      rounding per operation, no fused multiply-add (:63-68), then cast to the
  *      output dtype with round-to-nearest-even (`copy_`, :68).
+ *
+ *  oracle_rowwise_quant - tilegen/comfyui/backend.py:230-232, the
+ *      rotation-free branch, as torch evaluates it on CUDA for an fp16/bf16
+ *      x: absmax in x's dtype (exact; NaN propagates as torch's amax does),
+ *      .float() / 127.0 (a tensor divided by a host scalar: multiplied by the
+ *      fp32 reciprocal of 127), clamp_min(1e-30) (NaN kept); divisor
+ *      d = scale rounded to x's dtype; q = x / d in fp32 (IEEE) rounded to x's
+ *      dtype, round half to even, clamp to [-128, 127] (NaN kept), int8 cast
+ *      (NaN -> 0).
  *
  * Build with -ffp-contract=off: a contracted a*b+c would change the rounding.
  */
@@ -173,6 +182,40 @@ int oracle_rotate_quant(const void *x, int dtype, int64_t M, int64_t K, int grou
                 v = fminf(fmaxf(v, -128.0f), 127.0f);
                 q[m * K + g0 + i] = (int8_t)v;
             }
+        }
+    }
+    return 0;
+}
+
+static float round_to_dtype(float v, int dtype) {
+    return dtype == DT_BF16 ? bf16_to_f32(f32_to_bf16(v)) : f16_to_f32(f32_to_f16(v));
+}
+
+/* Returns 0 on success, -1 on a bad argument (dtype must be DT_F16 or DT_BF16). */
+int oracle_rowwise_quant(const void *x, int dtype, int64_t M, int64_t K, int8_t *q, float *scale) {
+    if ((dtype != DT_F16 && dtype != DT_BF16) || K <= 0 || M < 0) return -1;
+    const float inv127 = 1.0f / 127.0f;
+#pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m) {
+        float amax = 0.0f;
+        for (int64_t k = 0; k < K; ++k) {
+            const float a = fabsf(load_elem(x, dtype, m * K + k));
+            if (isnan(a) || isnan(amax)) amax = NAN;
+            else if (a > amax) amax = a;
+        }
+        float s = amax * inv127;
+        if (!isnan(s) && s < 1e-30f) s = 1e-30f;
+        scale[m] = s;
+        const float d = round_to_dtype(s, dtype);
+        for (int64_t k = 0; k < K; ++k) {
+            const float t = round_to_dtype(load_elem(x, dtype, m * K + k) / d, dtype);
+            float r = nearbyintf(t);
+            if (isnan(r)) {
+                q[m * K + k] = 0;
+                continue;
+            }
+            r = fminf(fmaxf(r, -128.0f), 127.0f);
+            q[m * K + k] = (int8_t)r;
         }
     }
     return 0;

@@ -15,6 +15,11 @@ records their outputs on small seeded inputs:
 * ``gemm.npz``    - ``tilegen.quant.int8_ops.int8_matmul_dequant_chunked``
   (int8_ops.py:22-70) through CPU ``torch._int_mm``: fp16/bf16/fp32 outputs,
   with and without bias, per-channel and scalar weight scales, small chunk caps.
+* ``rowwise.npz`` - the rotation-free branch of the production wrapper
+  (tilegen/comfyui/backend.py:230-232), executed from the reference file's own
+  two lines (the reference has no function for it) on fp16/bf16 inputs, with
+  an all-zero row, a row whose fp16 divisor underflows and near-max values.
+  ``--only rowwise`` writes just this file.
 * ``config1.npz`` - the CPU reference workload end to end: x fp32 [256, 5120]
   N(0,1) with 1 % outlier channels x30, W fp32 [5120, 5120] N(0, 0.02), seed 0;
   Y = dequant(int8 GEMM).  Stored: input checksums, both scale vectors, the
@@ -42,6 +47,60 @@ def _sha(t: torch.Tensor) -> str:
 def _u16(t: torch.Tensor) -> np.ndarray:
     """fp16/bf16 tensor -> its raw 16-bit patterns (numpy has no bf16)."""
     return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _split_absmax(dtype: torch.dtype, m: int) -> torch.Tensor:
+    """m values of ``dtype`` in [1, 256) whose fp32 a/127 and a*fp32(1/127) differ."""
+    bits = torch.arange(0, 0x7c00 if dtype == torch.float16 else 0x7f80, dtype=torch.int32)
+    vals = bits.to(torch.int16).view(dtype).float()
+    vals = vals[(vals >= 1) & (vals < 256)]
+    r = torch.tensor(1.0, dtype=torch.float32) / torch.tensor(127.0, dtype=torch.float32)
+    split = vals[vals / torch.tensor(127.0) != vals * r]
+    idx = torch.linspace(0, split.numel() - 1, m).long()
+    return split[idx]
+
+
+def rowwise(ref_root: str) -> None:
+    """Run backend.py:231-232 (the row-wise branch's two statements) on seeded inputs."""
+    sys.path.append(REPO)
+    from tilegen_b200.synthetic import outlier_activations
+
+    with open(os.path.join(ref_root, "tilegen", "comfyui", "backend.py")) as f:
+        lines = f.read().splitlines()[230:232]
+    assert lines[0].strip().startswith("xscale =") and lines[1].strip().startswith("xq ="), lines
+    code = compile("\n".join(ln.strip() for ln in lines), "backend.py:231-232", "exec")
+    dts = {"f16": torch.float16, "bf16": torch.bfloat16}
+    out = {}
+    cases = [
+        # name, M, K, dtype, seed
+        ("a", 8, 5120, "f16", 21),
+        ("b", 6, 13824, "bf16", 22),
+        ("c", 5, 320, "f16", 23),
+        ("d", 5, 64, "bf16", 24),
+        ("e", 6, 256, "f16", 25),
+        ("f", 6, 128, "bf16", 26),
+    ]
+    for name, m, k, dt, seed in cases:
+        x = outlier_activations(m, k, seed=seed, dtype=dts[dt])
+        if name in ("c", "d"):
+            x[0].zero_()                                      # all-zero row
+            x[1] = x[1].float().mul(1e-8).to(x.dtype)         # fp16 divisor underflows to 0
+            x[2] = x[2].float().mul(2000.0).clamp(-60000, 60000).to(x.dtype)
+            x[3] = x[3].float().mul(1e-7).to(x.dtype)         # fp16 divisor subnormal
+        if name in ("e", "f"):
+            # absmax values a with fp32(a / 127) != fp32(a * fp32(1/127)): torch's
+            # CPU divides, its CUDA kernel multiplies by the reciprocal.
+            x = (x.float() * 0.05).to(x.dtype)
+            a = _split_absmax(x.dtype, m)
+            x[torch.arange(m), torch.arange(m) * 5 + 3] = a.to(x.dtype)
+        ns = {"torch": torch, "x2d": x}
+        exec(code, ns)
+        out[f"{name}_meta"] = np.array([m, k, list(dts).index(dt) + 1], dtype=np.int64)
+        out[f"{name}_x"] = _u16(x)
+        out[f"{name}_q"] = ns["xq"].numpy()
+        out[f"{name}_scale"] = ns["xscale"].numpy()
+    np.savez_compressed(os.path.join(HERE, "rowwise.npz"), **out)
+    print("rowwise.npz", os.path.getsize(os.path.join(HERE, "rowwise.npz")), "bytes")
 
 
 def main(ref_root: str) -> None:
@@ -132,7 +191,13 @@ def main(ref_root: str) -> None:
     print("config1 rel-Frobenius vs fp32 dense:", rel)
     for f in ("quant.npz", "weight.npz", "gemm.npz", "config1.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
+    rowwise(ref_root)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    root = args[0] if args else "/root/reference"
+    if "--only" in sys.argv and sys.argv[-1] == "rowwise":
+        rowwise(root)
+    else:
+        main(root)

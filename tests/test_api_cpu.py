@@ -18,25 +18,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.conftest import GOLDEN, REPO
-
-FAKES = os.path.join(REPO, "tests", "fakes")
-
-
-@pytest.fixture
-def fake_kitchen(monkeypatch):
-    """Put the comfy_kitchen test double on the path with a fresh registry."""
-    monkeypatch.syspath_prepend(FAKES)
-    for name in [m for m in sys.modules if m == "comfy_kitchen" or m.startswith("comfy_kitchen.")]:
-        monkeypatch.delitem(sys.modules, name)
-    import comfy_kitchen.registry as reg
-
-    from tilegen_b200.comfyui import backend
-
-    monkeypatch.setattr(backend, "_INSTALLED", False)
-    monkeypatch.setattr(backend, "_FAILED_FHT_SHAPES", set())
-    yield reg.registry
-
+from tests.conftest import FAKES, GOLDEN, REPO
 
 # ---------------------------------------------------------------- hadamard
 def test_hadamard_orthonormal_and_symmetric():

@@ -97,3 +97,27 @@ def test_small_m_entry_points_check_before_device_work():
             _lib.TG_ERR_UNSUPPORTED
     assert L.tg_int8_gemm_dequant_splitk_noalloc(None, None, None, None, 1, None, 0, 0, 128, 64, 1, None,
                                                  None) == _lib.TG_OK
+
+
+def test_quantize_act_checks_before_device_work():
+    L = _lib.lib()
+    p = ctypes.c_void_p(16)
+    assert "tg_quantize_act" in _lib.declared_functions()
+    # unknown activation, unsupported group, K rules (256 rotated, 64 row-wise)
+    assert L.tg_quantize_act(p, _lib.TG_DT_F16, 4, 5120, 256, 3, p, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_quantize_act(p, _lib.TG_DT_F16, 4, 5120, 256, -1, p, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_quantize_act(p, _lib.TG_DT_F16, 4, 5120, 2, 0, p, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_quantize_act(p, _lib.TG_DT_F16, 4, 5120, 128, 1, p, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_quantize_act(p, _lib.TG_DT_F16, 4, 320, 256, 1, p, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_quantize_act(p, _lib.TG_DT_F16, 4, 96, 1, 0, p, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_quantize_act(p, _lib.TG_DT_F16, 4, 32832, 1, 0, p, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_quantize_act(p, _lib.TG_DT_F32, 4, 320, 1, 0, p, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_quantize_act(p, _lib.TG_DT_BF16, -1, 320, 1, 2, p, p, None) == _lib.TG_ERR_INVALID_ARG
+    # M == 0 is a no-op; null pointers with M > 0 are rejected; misaligned x
+    assert L.tg_quantize_act(None, _lib.TG_DT_F16, 0, 320, 1, 1, None, None, None) == _lib.TG_OK
+    assert L.tg_quantize_act(None, _lib.TG_DT_F16, 2, 320, 1, 1, None, None, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_quantize_act(ctypes.c_void_p(8), _lib.TG_DT_F16, 2, 320, 1, 1, p, p, None) == \
+        _lib.TG_ERR_MISALIGNED
+    # tg_rotate_quant keeps rejecting group 1 (the row-wise branch is tg_quantize_act's)
+    assert L.tg_rotate_quant(p, _lib.TG_DT_F16, 4, 320, 1, p, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_rotate_quant(p, _lib.TG_DT_F16, -1, 320, 1, p, p, None) == _lib.TG_ERR_INVALID_ARG

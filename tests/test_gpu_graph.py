@@ -49,3 +49,27 @@ def test_linear_replayed_from_a_cuda_graph(cuda, m, k, n):
         assert np.array_equal(out_bits(y), out_bits(ref)), f"replay {i}"
     del graph
     assert _lib.device_status(0) == 0
+
+
+@pytest.mark.parametrize("group,act", [(256, "gelu_tanh"), (1, "gelu"), (1, None)])
+def test_quantize_act_replayed_from_a_cuda_graph(cuda, group, act):
+    m, k = 1000, 13824
+    g = torch.Generator(device=cuda).manual_seed(group)
+    x = torch.empty(m, k, dtype=torch.bfloat16, device=cuda)
+    stream = torch.cuda.Stream(device=cuda)
+    with torch.cuda.stream(stream):
+        x.copy_(torch.randn(m, k, generator=g, device=cuda))
+        ops.quantize_act(x, group, act)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        q, s = ops.quantize_act(x, group, act)
+    for i in range(3):
+        x.copy_(torch.randn(m, k, generator=g, device=cuda) * (1 + i))
+        graph.replay()
+        torch.cuda.synchronize()
+        rq, rs = ops.quantize_act(x, group, act)
+        torch.cuda.synchronize()
+        assert torch.equal(q, rq) and torch.equal(s.view(torch.int32), rs.view(torch.int32)), f"replay {i}"
+    del graph
+    assert _lib.device_status(0) == 0

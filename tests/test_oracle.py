@@ -98,3 +98,43 @@ def test_rejects_bad_groups():
         oracle.rotate_quant(np.zeros((1, 256), np.float32), "float32", 128)
     with pytest.raises(ValueError):
         oracle.rotate_quant(np.zeros((1, 320), np.float32), "float32", 256)
+
+
+def _rowwise_cases():
+    d = np.load(os.path.join(GOLDEN, "rowwise.npz"))
+    for name in sorted({k.split("_")[0] for k in d.files}):
+        m, k, dt = (int(v) for v in d[f"{name}_meta"])
+        yield name, d[f"{name}_x"], ("float16" if dt == 1 else "bfloat16"), d[f"{name}_q"], d[f"{name}_scale"]
+
+
+def test_rowwise_matches_reference_lines():
+    """oracle_rowwise_quant vs backend.py:231-232 run by torch on the CPU.
+
+    Codes are identical.  Scales are identical except where torch's CPU kernel
+    and its CUDA kernel evaluate `amax.float() / 127.0` differently: the CPU
+    divides, CUDA multiplies by fp32(1/127), and the oracle restates the CUDA
+    evaluation (the product's device).  The fixtures plant absmax values where
+    the two differ; there the fixture must equal the division and the oracle
+    the reciprocal product, one ulp apart.
+    """
+    r = np.float32(1) / np.float32(127)
+    split_rows = 0
+    for name, x, dt, gq, gs in _rowwise_cases():
+        q, s = oracle.rowwise_quant(x, dt)
+        assert np.array_equal(q, gq), name
+        xf = torch.from_numpy(x.view(np.int16)).view(torch.float16 if dt == "float16" else torch.bfloat16)
+        amax = xf.float().abs().amax(dim=1).numpy()
+        div = np.maximum(amax / np.float32(127), np.float32(1e-30))
+        mul = np.maximum(amax * r, np.float32(1e-30))
+        assert np.array_equal(gs.view(np.uint32), div.view(np.uint32)), name
+        assert np.array_equal(s.view(np.uint32), mul.view(np.uint32)), name
+        split_rows += int(np.sum(div != mul))
+    assert split_rows >= 6  # the planted rows really separate the two evaluations
+
+
+def test_rowwise_planted_mistake_is_caught():
+    """A code off by one in the oracle's output would fail the fixture comparison."""
+    name, x, dt, gq, _ = next(_rowwise_cases())
+    q, _ = oracle.rowwise_quant(x, dt)
+    q[0, 0] = np.int8(q[0, 0] + (1 if q[0, 0] < 127 else -1))
+    assert not np.array_equal(q, gq)

@@ -10,7 +10,7 @@ import sys
 
 _MODULES = (
     "kernels", "kernels.hadamard", "kernels.int8_convrot",
-    "quant", "quant.weight", "quant.int8_ops",
+    "quant", "quant.weight", "quant.int8_ops", "quant.rowwise",
     "runtime", "runtime.device", "runtime.nvrtc",
     "comfyui", "comfyui.backend", "comfyui.nodes",
 )

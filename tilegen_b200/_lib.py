@@ -33,6 +33,7 @@ TG_ERR_CUDA = 4
 TG_ERR_DEVICE_TIMEOUT = 5
 
 TG_DT_F32, TG_DT_F16, TG_DT_BF16 = 0, 1, 2
+TG_ACT_NONE, TG_ACT_GELU_TANH, TG_ACT_GELU = 0, 1, 2
 
 _lock = threading.Lock()
 _lib = None
@@ -97,6 +98,8 @@ def lib() -> ctypes.CDLL:
         L.tg_rotate_quant.argtypes = [p, i32, i64, i64, i32, p, p, p]
         L.tg_rotate_quant.restype = i32
         L.tg_rotate_quant_max_k.restype = i64
+        L.tg_quantize_act.argtypes = [p, i32, i64, i64, i32, i32, p, p, p]
+        L.tg_quantize_act.restype = i32
         L.tg_int8_gemm_dequant.argtypes = [p, p, p, p, i64, p, i32, i64, i64, i64, i32, p, p]
         L.tg_int8_gemm_dequant.restype = i32
         L.tg_gemm_config.argtypes = [i64, i64, ctypes.POINTER(i32), ctypes.POINTER(i32)]

@@ -104,6 +104,15 @@ def _eager_quantize_convrot(x: torch.Tensor, group_size: int):
     return q, scale
 
 
+def _apply_act(x: torch.Tensor, act: str | None) -> torch.Tensor:
+    """The unfused input activation (comfy_kitchen's ``apply_input_act``)."""
+    if act is None:
+        return x
+    from comfy_kitchen.backends._activations import apply_input_act
+
+    return apply_input_act(x, act)
+
+
 def _kernel_accepts(x: torch.Tensor, group_size: int) -> bool:
     from ..kernels.int8_convrot import can_use_fht
 
@@ -180,27 +189,45 @@ def int8_linear(
 
         return eager_int8_linear(x, weight, weight_scale, bias=bias, out_dtype=out_dtype, convrot=convrot,
                                  convrot_groupsize=convrot_groupsize, input_act=input_act)
-    if input_act not in (None, "none"):
+    # input_act (backend.py:201-204): the activations the quantiser fuses are
+    # applied inside it on the kernel paths; any other goes through
+    # comfy_kitchen first, and every fallback applies it unfused, as the
+    # reference does.
+    from ..ops import FUSED_ACTS
+
+    act = None if input_act in (None, "none") else input_act
+    if act is not None and act not in FUSED_ACTS:
         from comfy_kitchen.backends._activations import apply_input_act
 
-        x = apply_input_act(x, input_act)
+        x = apply_input_act(x, act)
+        act = None
     shape = tuple(x.shape)
     x2d = x.reshape(-1, x.shape[-1]).contiguous()
     weight = weight.to(device=x.device, dtype=torch.int8)
-    if x2d.shape[1] % convrot_groupsize:
-        raise ValueError(f"ConvRot group size {convrot_groupsize} does not divide K={x2d.shape[1]}")
-    key = (x2d.shape[0], x2d.shape[1], x2d.dtype, x2d.device.index)
-    if _can_use_fht(x2d, convrot_groupsize, mode) and key not in _FAILED_FHT_SHAPES:
-        try:
-            from ..kernels.int8_convrot import quantize_convrot_fht
+    if convrot:
+        if x2d.shape[1] % convrot_groupsize:
+            raise ValueError(f"ConvRot group size {convrot_groupsize} does not divide K={x2d.shape[1]}")
+        key = (x2d.shape[0], x2d.shape[1], x2d.dtype, x2d.device.index)
+        if _can_use_fht(x2d, convrot_groupsize, mode) and key not in _FAILED_FHT_SHAPES:
+            try:
+                if act is None:
+                    from ..kernels.int8_convrot import quantize_convrot_fht
 
-            xq, xscale = quantize_convrot_fht(x2d, convrot_groupsize)
-        except Exception:  # a shape the kernel rejects: remember it, use eager
-            _FAILED_FHT_SHAPES.add(key)
-            LOGGER.exception("FHT failed for M=%d K=%d; using eager ConvRot", x2d.shape[0], x2d.shape[1])
-            xq, xscale = _eager_quantize_convrot(x2d, convrot_groupsize)
+                    xq, xscale = quantize_convrot_fht(x2d, convrot_groupsize)
+                else:
+                    from ..ops import quantize_act
+
+                    xq, xscale = quantize_act(x2d, convrot_groupsize, act)
+            except Exception:  # a shape the kernel rejects: remember it, use eager
+                _FAILED_FHT_SHAPES.add(key)
+                LOGGER.exception("FHT failed for M=%d K=%d; using eager ConvRot", x2d.shape[0], x2d.shape[1])
+                xq, xscale = _eager_quantize_convrot(_apply_act(x2d, act), convrot_groupsize)
+        else:
+            xq, xscale = _eager_quantize_convrot(_apply_act(x2d, act), convrot_groupsize)
     else:
-        xq, xscale = _eager_quantize_convrot(x2d, convrot_groupsize)
+        from ..quant.rowwise import quantize_rowwise
+
+        xq, xscale = quantize_rowwise(x2d, act)
     max_temp_mb = max(16, int(os.environ.get("TILEGEN_INT8_TEMP_MB", "256")))
     out = int8_matmul_dequant_chunked(xq, xscale, weight, weight_scale, bias, out_dtype,
                                       max_temp_bytes=max_temp_mb * 1024 * 1024)

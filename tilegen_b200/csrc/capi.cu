@@ -75,12 +75,12 @@ bool ensure_smem_attr(K kernel, int dev, uint32_t bytes, uint32_t* done_bytes) {
 }
 
 // ------------------------------------------------------------------ rotate+quant
-template <int NST, bool BF16>
+template <int NST, bool BF16, int ACT>
 int launch_rotquant_t(const CUtensorMap& tm, const tg::RotQuantParams& p, int threads, uint32_t smem, int dev,
                       int sms, cudaStream_t st) {
   static uint32_t attr_done[kMaxDevices];
   static int occ_cache[kMaxDevices][4][2];  // [dev][stages-1..][threads>256]
-  auto kern = tg::rotquant_kernel<NST, BF16>;
+  auto kern = tg::rotquant_kernel<NST, BF16, ACT>;
   if (!ensure_smem_attr(kern, dev, smem, attr_done)) return TG_ERR_CUDA;
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem) != cudaSuccess || occ < 1)
@@ -99,6 +99,16 @@ int launch_rotquant_t(const CUtensorMap& tm, const tg::RotQuantParams& p, int th
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, tm, p) != cudaSuccess) return TG_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
+}
+
+template <int NST, bool BF16>
+int launch_rotquant_act(int act, const CUtensorMap& tm, const tg::RotQuantParams& p, int threads, uint32_t smem,
+                        int dev, int sms, cudaStream_t st) {
+  switch (act) {
+    case TG_ACT_GELU_TANH: return launch_rotquant_t<NST, BF16, tg::kActGeluTanh>(tm, p, threads, smem, dev, sms, st);
+    case TG_ACT_GELU: return launch_rotquant_t<NST, BF16, tg::kActGelu>(tm, p, threads, smem, dev, sms, st);
+    default: return launch_rotquant_t<NST, BF16, tg::kActNone>(tm, p, threads, smem, dev, sms, st);
+  }
 }
 
 int gcd_int(int a, int b) {
@@ -132,17 +142,30 @@ int64_t tg_rotate_quant_max_k(void) { return kRotQuantMaxK; }
 
 int tg_rotate_quant(const void* x, int x_dtype, int64_t M, int64_t K, int group, int8_t* q, float* scale,
                     void* stream) {
+  if (group == 1) {  // the rotation-free branch is tg_quantize_act's
+    if (M < 0 || K <= 0 || (x_dtype != TG_DT_F16 && x_dtype != TG_DT_BF16)) return TG_ERR_INVALID_ARG;
+    return TG_ERR_UNSUPPORTED;
+  }
+  return tg_quantize_act(x, x_dtype, M, K, group, TG_ACT_NONE, q, scale, stream);
+}
+
+int tg_quantize_act(const void* x, int x_dtype, int64_t M, int64_t K, int group, int act, int8_t* q, float* scale,
+                    void* stream) {
   if (M < 0 || K <= 0) return TG_ERR_INVALID_ARG;
   if (x_dtype != TG_DT_F16 && x_dtype != TG_DT_BF16) return TG_ERR_INVALID_ARG;
+  if (act != TG_ACT_NONE && act != TG_ACT_GELU_TANH && act != TG_ACT_GELU) return TG_ERR_INVALID_ARG;
   int nst;
   switch (group) {
+    case 1: nst = 0; break;
     case 4: nst = 1; break;
     case 16: nst = 2; break;
     case 64: nst = 3; break;
     case 256: nst = 4; break;
     default: return TG_ERR_UNSUPPORTED;
   }
-  if (K % 256 != 0 || K > kRotQuantMaxK) return TG_ERR_UNSUPPORTED;
+  // Rotated: K % 256 as the reference launcher requires (int8_convrot.py:196-230).
+  // Row-wise: whole 64-element lines (one thread owns one).
+  if (K % (nst == 0 ? 64 : 256) != 0 || K > kRotQuantMaxK) return TG_ERR_UNSUPPORTED;
   if (M == 0) return TG_OK;
   if (!x || !q || !scale) return TG_ERR_INVALID_ARG;
   if (!aligned16(x) || !aligned16(q) || (reinterpret_cast<uintptr_t>(scale) & 3u)) return TG_ERR_MISALIGNED;
@@ -209,16 +232,20 @@ int tg_rotate_quant(const void* x, int x_dtype, int64_t M, int64_t K, int group,
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf = x_dtype == TG_DT_BF16;
+#define TG_RQ_CASE(N)                                                                        \
+  case N:                                                                                    \
+    return bf ? launch_rotquant_act<N, true>(act, tm, p, threads, smem, dev, info.sms, st) \
+              : launch_rotquant_act<N, false>(act, tm, p, threads, smem, dev, info.sms, st);
   switch (nst) {
-    case 1: return bf ? launch_rotquant_t<1, true>(tm, p, threads, smem, dev, info.sms, st)
-                      : launch_rotquant_t<1, false>(tm, p, threads, smem, dev, info.sms, st);
-    case 2: return bf ? launch_rotquant_t<2, true>(tm, p, threads, smem, dev, info.sms, st)
-                      : launch_rotquant_t<2, false>(tm, p, threads, smem, dev, info.sms, st);
-    case 3: return bf ? launch_rotquant_t<3, true>(tm, p, threads, smem, dev, info.sms, st)
-                      : launch_rotquant_t<3, false>(tm, p, threads, smem, dev, info.sms, st);
-    default: return bf ? launch_rotquant_t<4, true>(tm, p, threads, smem, dev, info.sms, st)
-                       : launch_rotquant_t<4, false>(tm, p, threads, smem, dev, info.sms, st);
+    TG_RQ_CASE(0)
+    TG_RQ_CASE(1)
+    TG_RQ_CASE(2)
+    TG_RQ_CASE(3)
+    default:
+      return bf ? launch_rotquant_act<4, true>(act, tm, p, threads, smem, dev, info.sms, st)
+                : launch_rotquant_act<4, false>(act, tm, p, threads, smem, dev, info.sms, st);
   }
+#undef TG_RQ_CASE
 }
 
 }  // extern "C"

@@ -23,6 +23,16 @@
 //  * Row absmax: warp shuffles over the row's lanes, then one shared-memory
 //    atomicMax per segment and a CTA barrier.  The rotated values never leave
 //    registers; the codes are packed 16 per 128-bit store straight to HBM.
+//
+// Two prologue/branch options of the production wrapper
+// (tilegen/comfyui/backend.py:166-244) run inside the same pass:
+//  * ACT: an elementwise input activation applied to x before anything else
+//    (backend.py:201-204), evaluated in fp32 and rounded back to x's dtype as
+//    the separate elementwise op it replaces would store it;
+//  * NST == 0: no rotation -- the row-wise int8 branch of backend.py:230-232,
+//    with that branch's torch arithmetic (scale = absmax * fp32(1/127) clamped
+//    at 1e-30, codes = int8(clamp(round(dtype(x / dtype(scale))), -128, 127)),
+//    NaN propagating through absmax as torch's amax does).
 #pragma once
 
 #include "common.cuh"
@@ -90,6 +100,14 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
   return r;
 }
 
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+
 // bfly4 on two independent butterflies at once (lanes .x and .y).
 __device__ __forceinline__ void bfly4x2(float2& a0, float2& a1, float2& a2, float2& a3) {
   const float2 s = add2(a0, a1);
@@ -132,17 +150,69 @@ __device__ __forceinline__ void stage2_64(float2 (&vp)[32]) {
   for (int l = 0; l < 8; ++l) bfly4x2(vp[l], vp[l + 8], vp[l + 16], vp[l + 24]);
 }
 
+// Input activations (the names of backend.py's `input_act`).
+enum : int { kActNone = 0, kActGeluTanh = 1, kActGelu = 2 };
+
+// The activation in fp32, written as torch's CUDA GELU kernels evaluate it in
+// their fp32 op-math (the same expression, so the same contractions and the
+// same tanhf/erff calls):
+//   gelu_tanh(x) = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+//   gelu(x)      = x 0.5 (1 + erf(x / sqrt(2)))
+template <int ACT>
+__device__ __forceinline__ float act_f32(float x) {
+  if (ACT == kActGeluTanh) {
+    constexpr float kBeta = float(1.41421356237309504880 * 1.12837916709551257390 * 0.5);
+    constexpr float kKappa = 0.044715f;
+    const float x_cube = x * x * x;
+    const float inner = kBeta * (x + kKappa * x_cube);
+    return 0.5f * x * (1.0f + tanhf(inner));
+  } else if (ACT == kActGelu) {
+    constexpr float kAlpha = float(0.70710678118654752440);
+    return x * 0.5f * (1.0f + erff(x * kAlpha));
+  }
+  return x;
+}
+
+// fp32 -> x's dtype -> fp32 (round to nearest even), as a store to an
+// fp16/bf16 tensor and the next op's load do.
 template <bool BF16>
+__device__ __forceinline__ float round_to_dtype(float v) {
+  return BF16 ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
+}
+
+// The same for a pair, as one packed conversion (cvt.rn.{f16,bf16}x2.f32).
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2_dtype(float2 v) {
+  if (BF16) {
+    const __nv_bfloat162 h = __float22bfloat162_rn(v);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  const __half2 h = __float22half2_rn(v);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2_dtype(uint32_t u) {
+  if (BF16) return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+  return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
+
+template <bool BF16, int ACT>
 __device__ __forceinline__ void unpack8(const uint4 w, float2* f) {
   const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    if (BF16) {
-      f[i] = make_float2(__uint_as_float(u[i] << 16), __uint_as_float(u[i] & 0xffff0000u));
-    } else {
-      f[i] = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
-    }
+    f[i] = unpack2_dtype<BF16>(u[i]);
+    if (ACT != kActNone)
+      f[i] = unpack2_dtype<BF16>(pack2_dtype<BF16>(make_float2(act_f32<ACT>(f[i].x), act_f32<ACT>(f[i].y))));
   }
+}
+
+// NaN-propagating max (torch's amax), and max(m, |a|, |b|) in that sense.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 
 // Codes for two values, each returned in the low byte of its word:
@@ -165,7 +235,56 @@ __device__ __forceinline__ uint32_t pack4(uint2 a, uint2 b) {
   return __byte_perm(__byte_perm(a.x, a.y, 0x0040), __byte_perm(b.x, b.y, 0x0040), 0x5410);
 }
 
-template <int NST, bool BF16>
+// Codes of the rotation-free branch: int8(clamp(round(dtype(v / d)), -128, 127))
+// with d the scale rounded to x's dtype, the division IEEE fp32 (torch's
+// op-math), dtype() rounding to x's dtype, round() half to even, clamp keeping
+// NaN and the int8 cast of NaN giving 0.  Returned in the low byte of a word.
+//
+// General form, for rows whose d is 0 (fp16 underflow: 0/0 is NaN), inf or NaN.
+template <bool BF16>
+__device__ __forceinline__ uint32_t rowwise_code(float v, float d) {
+  const float t = round_to_dtype<BF16>(__fdiv_rn(v, d));
+  const float r = rintf(t);
+  if (r != r) return 0u;
+  return uint32_t(int(fminf(fmaxf(r, -128.0f), 127.0f)));
+}
+
+// Fast form for a finite, non-zero d, four values at a time (a.x, a.y, b.x,
+// b.y -> bytes 0..3).  The quotient: q0 = RN(v * rcp) with rcp = RN(1/d) is
+// within one ulp of v/d, the remainder v - q0*d is exact as one FMA, and
+// RN(q0 + rem * rcp) is the correctly rounded v/d (Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990; quotients small enough to underflow give code 0 either
+// way).  |v| <= absmax <= 127 d (1 + 2^-8) keeps |q| < 128.5, so no NaN or
+// inf occurs.  The packed dtype rounding, then clamp, then round half to even:
+// fp16 adds 1536 (spacing 1 in [1024, 2048), so the add is the rounding and
+// the low byte of the sum's bits is the code); bf16, whose spacing is too
+// coarse for that, rounds in fp32 with 1.5 * 2^23.  Clamping first equals
+// torch's round-then-clamp because the bounds are integers.
+template <bool BF16>
+__device__ __forceinline__ uint32_t rowwise_codes4(float2 a, float2 b, float2 rcp2, float2 nd2) {
+  float2 qa = mul2(a, rcp2), qb = mul2(b, rcp2);
+  qa = fma2(fma2(qa, nd2, a), rcp2, qa);
+  qb = fma2(fma2(qb, nd2, b), rcp2, qb);
+  if (BF16) {
+    const __nv_bfloat162 lo = __float2bfloat162_rn(-128.0f), hi = __float2bfloat162_rn(127.0f);
+    __nv_bfloat162 ha = __float22bfloat162_rn(qa), hb = __float22bfloat162_rn(qb);
+    ha = __hmin2(__hmax2(ha, lo), hi);
+    hb = __hmin2(__hmax2(hb, lo), hi);
+    const float2 magic = make_float2(12582912.0f, 12582912.0f);
+    const float2 fa = add2(unpack2_dtype<true>(*reinterpret_cast<const uint32_t*>(&ha)), magic);
+    const float2 fb = add2(unpack2_dtype<true>(*reinterpret_cast<const uint32_t*>(&hb)), magic);
+    return pack4(make_uint2(__float_as_uint(fa.x), __float_as_uint(fa.y)),
+                 make_uint2(__float_as_uint(fb.x), __float_as_uint(fb.y)));
+  }
+  const __half2 lo = __float2half2_rn(-128.0f), hi = __float2half2_rn(127.0f), magic = __float2half2_rn(1536.0f);
+  __half2 ha = __float22half2_rn(qa), hb = __float22half2_rn(qb);
+  ha = __hadd2(__hmin2(__hmax2(ha, lo), hi), magic);
+  hb = __hadd2(__hmin2(__hmax2(hb, lo), hi), magic);
+  return __byte_perm(*reinterpret_cast<const uint32_t*>(&ha), *reinterpret_cast<const uint32_t*>(&hb), 0x6420);
+}
+
+template <int NST, bool BF16, int ACT>
 __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
                                                        const RotQuantParams p) {
   constexpr float kRoot = float(1 << NST);               // sqrt(G)
@@ -264,10 +383,10 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 w = *reinterpret_cast<const uint4*>(buf + (line_off ^ uint32_t(c << 4)));
-        unpack8<BF16>(w, &vp[4 * c]);
+        unpack8<BF16, ACT>(w, &vp[4 * c]);
       }
     }
-    stage0_64(vp);
+    if (NST >= 1) stage0_64(vp);
     if (NST >= 2) stage1_64(vp);
     if (NST >= 3) stage2_64(vp);
 
@@ -304,6 +423,12 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
         for (int r = 0; r < 4; ++r) am4[r] = absmax3(am4[r], w2[r][jp].x, w2[r][jp].y);
       }
       amax = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
+    } else if (NST == 0) {
+      float am4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        am4[i & 3] = max_nan(max_nan(am4[i & 3], fabsf(vp[i].x)), fabsf(vp[i].y));
+      amax = max_nan(max_nan(am4[0], am4[1]), max_nan(am4[2], am4[3]));
     } else {
       float am4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
@@ -312,7 +437,12 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
     }
 
     // ---- row absmax -----------------------------------------------------------
-    for (int o = 1; o < seg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    // (NST == 0: a NaN wins; its sign bit is clear after fabsf, so its bit
+    // pattern also wins the unsigned atomicMax below.)
+    for (int o = 1; o < seg; o <<= 1) {
+      const float other = __shfl_xor_sync(0xffffffffu, amax, o);
+      amax = NST == 0 ? max_nan(amax, other) : fmaxf(amax, other);
+    }
     unsigned* rm = rowmax + rm_cur * R;
     if (active && (lane & (seg - 1)) == 0) atomicMax(&rm[row_local], __float_as_uint(amax));
     __syncthreads();
@@ -329,7 +459,39 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
     if (tid < R) rowmax[rm_clear * R + tid] = 0u;
 
     const int row = batch * R + row_local;
-    if (active && row < M) {
+    if (NST == 0 && active && row < M) {
+      // backend.py:230: (amax.float() / 127.0).clamp_min(1e-30); torch divides
+      // a CUDA tensor by a host scalar as a multiply by its fp32 reciprocal.
+      const float am = __uint_as_float(rm[row_local]);
+      float sc = __fmul_rn(am, 1.0f / 127.0f);
+      sc = sc != sc ? sc : fmaxf(sc, 1e-30f);
+      if (chunk == 0) sout[row] = sc;
+      const float d = round_to_dtype<BF16>(sc);  // scale[:, None].to(x.dtype)
+      int8_t* qp = qout + size_t(row) * size_t(K) + code_off;
+      if (d > 0.0f && d < __int_as_float(0x7f800000)) {  // finite, non-zero
+        const float rcp = __frcp_rn(d);
+        const float2 rcp2 = make_float2(rcp, rcp), nd2 = make_float2(-d, -d);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t wd[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) wd[k] = rowwise_codes4<BF16>(vp[8 * c + 2 * k], vp[8 * c + 2 * k + 1], rcp2, nd2);
+          *reinterpret_cast<uint4*>(qp + c * 16) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t wd[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int i = 8 * c + 2 * k;  // pair index of value 16c + 4k
+            wd[k] = pack4(make_uint2(rowwise_code<BF16>(vp[i].x, d), rowwise_code<BF16>(vp[i].y, d)),
+                          make_uint2(rowwise_code<BF16>(vp[i + 1].x, d), rowwise_code<BF16>(vp[i + 1].y, d)));
+          }
+          *reinterpret_cast<uint4*>(qp + c * 16) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        }
+      }
+    } else if (NST != 0 && active && row < M) {
       const float am = __uint_as_float(rm[row_local]);
       const float sc = fmaxf(__fdiv_rn(am, kQmaxRoot), 1e-30f);
       if (chunk == 0) sout[row] = sc;

@@ -1,15 +1,16 @@
 """Torch-facing wrappers over the C ABI, plus their ``torch.library`` custom ops.
 
-``rotate_quant`` and ``int8_gemm_dequant`` allocate their outputs with torch's
+``rotate_quant``, ``quantize_act`` and ``int8_gemm_dequant`` allocate their outputs with torch's
 caching allocator and enqueue the sm_100a kernels on the current stream of the
 input's device.  They never fall back to another implementation: an input the
 kernels do not handle raises ``ValueError``, a CUDA failure raises
 ``TileGenError``.  ``int8_gemm_dequant`` with few rows (see ``SPLITK_MAX_M``)
 uses the split-K kernel and a cached, self-clearing scratch per (device, stream).
 
-The same two functions are registered as ``torch.ops.tilegen.rotate_quant`` and
-``torch.ops.tilegen.int8_gemm_dequant`` (with fake implementations, so they
-trace under ``torch.compile``/``torch.export`` as opaque ops).
+The same functions are registered as ``torch.ops.tilegen.rotate_quant``,
+``torch.ops.tilegen.quantize_act`` and ``torch.ops.tilegen.int8_gemm_dequant``
+(with fake implementations, so they trace under ``torch.compile``/``torch.export``
+as opaque ops).
 """
 from __future__ import annotations
 
@@ -23,6 +24,8 @@ _DTYPE_CODE = {
     torch.bfloat16: _lib.TG_DT_BF16,
 }
 _SUPPORTED_GROUPS = (4, 16, 64, 256)
+# input_act names (tilegen/comfyui/backend.py:174) the quantiser applies itself.
+FUSED_ACTS = {"gelu_tanh": _lib.TG_ACT_GELU_TANH, "gelu": _lib.TG_ACT_GELU}
 
 
 def _aligned(t: torch.Tensor) -> torch.Tensor:
@@ -71,6 +74,42 @@ def rotate_quant(x: torch.Tensor, group: int = 256):
     s = torch.empty((m,), dtype=torch.float32, device=x.device)
     if m:
         _call("tg_rotate_quant", x.device, x.data_ptr(), _DTYPE_CODE[x.dtype], m, k, int(group),
+              q.data_ptr(), s.data_ptr())
+    return q, s
+
+
+def quantize_act(x: torch.Tensor, group: int = 256, act: str | None = None):
+    """``act`` applied to ``x [M, K]``, then rotate+quantise (``group`` 4..256) or,
+    with ``group=1``, the rotation-free row-wise quantisation of
+    tilegen/comfyui/backend.py:230-232.  One pass over ``x`` (``tg_quantize_act``).
+
+    ``act``: None/``"none"``, or a name in ``FUSED_ACTS``; the activation is what
+    torch's ``F.gelu`` (``approximate="tanh"`` for ``gelu_tanh``) stores for an
+    fp16/bf16 tensor.  Returns ``(q int8 [M, K], scale fp32 [M])``.  ``K`` must be
+    a multiple of 256 (of 64 for ``group=1``).
+    """
+    if not isinstance(x, torch.Tensor) or not x.is_cuda:
+        raise ValueError("quantize_act: CUDA tensor required")
+    if x.ndim != 2:
+        raise ValueError(f"quantize_act: expected 2-D input, got {tuple(x.shape)}")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"quantize_act: fp16/bf16 input required, got {x.dtype}")
+    if group != 1 and group not in _SUPPORTED_GROUPS:
+        raise ValueError(f"quantize_act: group must be 1 or one of {_SUPPORTED_GROUPS}, got {group}")
+    if act in (None, "none"):
+        code = _lib.TG_ACT_NONE
+    elif act in FUSED_ACTS:
+        code = FUSED_ACTS[act]
+    else:
+        raise ValueError(f"quantize_act: activation {act!r} is not one of {sorted(FUSED_ACTS)}")
+    m, k = x.shape
+    if k % (64 if group == 1 else 256):
+        raise ValueError(f"quantize_act: K={k} must be a multiple of {64 if group == 1 else 256}")
+    x = _aligned(x)
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m,), dtype=torch.float32, device=x.device)
+    if m:
+        _call("tg_quantize_act", x.device, x.data_ptr(), _DTYPE_CODE[x.dtype], m, k, int(group), code,
               q.data_ptr(), s.data_ptr())
     return q, s
 
@@ -164,6 +203,16 @@ def _rotate_quant_op(x: torch.Tensor, group: int) -> tuple[torch.Tensor, torch.T
 
 @_rotate_quant_op.register_fake
 def _(x, group):
+    return x.new_empty(x.shape, dtype=torch.int8), x.new_empty((x.shape[0],), dtype=torch.float32)
+
+
+@torch.library.custom_op("tilegen::quantize_act", mutates_args=())
+def _quantize_act_op(x: torch.Tensor, group: int, act: str | None) -> tuple[torch.Tensor, torch.Tensor]:
+    return quantize_act(x, group, act)
+
+
+@_quantize_act_op.register_fake
+def _(x, group, act):
     return x.new_empty(x.shape, dtype=torch.int8), x.new_empty((x.shape[0],), dtype=torch.float32)
 
 

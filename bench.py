@@ -350,6 +350,61 @@ def _quant_sweep(dev, flush, stream, iters=10):
     return rows
 
 
+def _input_act_table(dev, flush, stream, iters=20):
+    """ffn_down with its input activation (tilegen/comfyui/backend.py:201-204) at
+    M = 4096: gelu_tanh fused into the quantiser vs applied as its own op first,
+    for the quantiser alone and the whole linear (bf16 comparator: gelu then
+    cuBLAS); and the rotation-free row-wise quantiser (backend.py:230-232)."""
+    import torch
+    import torch.nn.functional as F
+
+    from tilegen_b200 import ops
+    from tilegen_b200.synthetic import gaussian_weight, outlier_activations
+
+    hbm = _peaks()[0]["hbm_gbs"]
+    m, k, n = M_PER_RANK, 13824, 5120
+
+    def timed(body):
+        def f(e):
+            e[0].record(stream)
+            body()
+            e[1].record(stream)
+
+        for _ in range(3):
+            f([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+        return round(statistics.mean(r[0] for r in _time_steps(f, iters, flush, stream)) * 1e3, 2)
+
+    act_rows = []
+    w = gaussian_weight(n, k, seed=1, dtype=torch.bfloat16, device=dev)
+    wq, ws = ops.rotate_quant(w, GROUP)
+    for dt in (torch.float16, torch.bfloat16):
+        x = outlier_activations(m, k, seed=0, dtype=dt, device=dev)  # pre-activation
+        wb = w.to(dt)
+        row = {"dtype": "fp16" if dt == torch.float16 else "bf16", "act": "gelu_tanh", "M": m, "K": k, "N": n}
+        row["quant_fused_us"] = timed(lambda: ops.quantize_act(x, GROUP, "gelu_tanh"))
+        row["quant_unfused_us"] = timed(lambda: ops.rotate_quant(F.gelu(x, approximate="tanh"), GROUP))
+        row["linear_fused_us"] = timed(
+            lambda: ops.int8_gemm_dequant(*ops.quantize_act(x, GROUP, "gelu_tanh"), wq, ws, None, dt))
+        row["linear_unfused_us"] = timed(
+            lambda: ops.int8_gemm_dequant(*ops.rotate_quant(F.gelu(x, approximate="tanh"), GROUP), wq, ws, None, dt))
+        row["bf16_gelu_cublas_us"] = timed(lambda: F.linear(F.gelu(x, approximate="tanh"), wb))
+        row["speedup_vs_bf16"] = round(row["bf16_gelu_cublas_us"] / row["linear_fused_us"], 3)
+        act_rows.append(row)
+        del x, wb
+    del w, wq, ws
+
+    rw_rows = []
+    for kk, mm in ((5120, 4096), (13824, 4096), (5120, 65536), (13824, 32768)):
+        for dt in (torch.float16, torch.bfloat16):
+            x = outlier_activations(mm, kk, seed=0, dtype=dt, device=dev)
+            us = timed(lambda: ops.quantize_act(x, 1, None))
+            gbs = (mm * kk * 3 + 4 * mm) / (us * 1e-6) / 1e9
+            rw_rows.append([kk, mm, "fp16" if dt == torch.float16 else "bf16", us, round(gbs, 1),
+                            round(gbs / hbm, 4)])
+            del x
+    return act_rows, rw_rows
+
+
 def _dit_block_bf16(dev, flush, stream, world, rank, tokens=65520, iters=10):
     """The DiT projection set on bf16 activations, `tokens` rows sharded over the ranks:
     per shape the max-over-ranks int8 linear and bf16 cuBLAS times and aggregate tokens/s."""
@@ -487,10 +542,11 @@ def run_tilegen(args):
     int8_lib_tops = _int_mm_tops(dev)
     status = _lib.device_status(local)
 
-    shapes = cpu = sweep = None
+    shapes = cpu = sweep = act_table = None
     if world == 1:
         shapes = _shape_table(dev, flush, stream)
         sweep = _quant_sweep(dev, flush, stream)
+        act_table = _input_act_table(dev, flush, stream)
     # Last: seconds of sustained load that leave the GPU at its power cap.
     if world > 1:
         dist.barrier()
@@ -554,6 +610,9 @@ def run_tilegen(args):
     line["dit_block_bf16"] = {"tokens": 65520, "rows_sharded_over": world, "shapes": block}
     if sweep is not None:
         line["quant_sweep"] = {"columns": ["group", "K", "M", "dtype", "us", "GB/s", "frac_of_hbm"], "rows": sweep}
+    if act_table is not None:
+        line["input_act_ffn_down"] = act_table[0]
+        line["rowwise_quant"] = {"columns": ["K", "M", "dtype", "us", "GB/s", "frac_of_hbm"], "rows": act_table[1]}
     print(json.dumps(line), flush=True)
 
 

@@ -515,11 +515,21 @@ def run_tilegen(args):
         return
 
     # ---- end to end through the public API, host buffers, copies timed ----
+    # The host-buffer linear (tilegen_b200.streaming.int8_linear_host: row chunks,
+    # H2D / kernels / D2H overlapped on three streams), and for reference the same
+    # copies and calls issued one after another on one stream.
+    from tilegen_b200.streaming import int8_linear_host
+
     x_host = x.cpu().pin_memory()
     out_host = torch.empty((m, n), dtype=torch.float16).pin_memory()
     x_dev = torch.empty_like(x)
 
     def e2e_step(e):
+        e[0].record(stream)
+        int8_linear_host(x_host, wq, ws, None, torch.float16, out=out_host, group_size=GROUP)
+        e[1].record(stream)
+
+    def e2e_serial_step(e):
         e[0].record(stream)
         x_dev.copy_(x_host, non_blocking=True)
         xq, xs = quantize_convrot(x_dev, GROUP, backend="fht")
@@ -527,15 +537,23 @@ def run_tilegen(args):
         out_host.copy_(y, non_blocking=True)
         e[1].record(stream)
 
-    for _ in range(3):
-        e2e_step([torch.cuda.Event(enable_timing=True) for _ in range(2)])
-    if world > 1:
-        dist.barrier()
-    te = _time_steps(e2e_step, max(3, min(args.steps, 50)), flush, stream)
-    e2e_total = torch.tensor([sum(r[0] for r in te)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
-    e2e_us = float(e2e_total.item()) * 1e3 / (world * len(te))
+    def e2e_time(fn):
+        for _ in range(3):
+            fn([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+        if world > 1:
+            dist.barrier()
+        te = _time_steps(fn, max(3, min(args.steps, 50)), flush, stream)
+        tot = torch.tensor([sum(r[0] for r in te)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+        return float(tot.item()) * 1e3 / (world * len(te))
+
+    e2e_us = e2e_time(e2e_step)
+    e2e_serial_us = e2e_time(e2e_serial_step)
+    ref_out = out_host.clone()
+    e2e_step([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+    torch.cuda.synchronize()
+    e2e_bitexact = bool(torch.equal(out_host.view(torch.int16), ref_out.view(torch.int16)))
 
     # ---- comparators ----
     bf16_us = _bf16_linear_us(x, w, max(5, min(args.steps, 50)), flush, stream)
@@ -597,8 +615,13 @@ def run_tilegen(args):
                            "traffic": QUANT_TRAFFIC_BYTES},
         "e2e": {"value": round(e2e_us, 2), "unit": "us", "h2d_bytes_per_step": x.numel() * 2,
                 "d2h_bytes_per_step": m * n * 2,
-                "path": "pinned host x -> tilegen.kernels.quantize_convrot -> tilegen.quant.int8_matmul_dequant_chunked -> pinned host out"},
-        "gpu_launches": 2 * args.steps,  # rotquant_kernel + gemm_i8_dequant_kernel per step
+                "path": "pinned host x -> tilegen_b200.streaming.int8_linear_host (512-row chunks: H2D, "
+                        "rotate+quant + GEMM, D2H on three streams) -> pinned host out",
+                "serial_us": round(e2e_serial_us, 2),
+                "serial_path": "one stream: H2D of x, tilegen.kernels.quantize_convrot, "
+                               "tilegen.quant.int8_matmul_dequant_chunked, D2H of the output",
+                "bit_identical_to_serial": e2e_bitexact},
+        "gpu_launches": 2 * args.steps,  # rotquant_kernel + gemm_i8_dequant_kernel per step (timed region)
         "clocks": clocks,
         "device_status": status,
         "wall_s_timed_region": round(wall, 3),

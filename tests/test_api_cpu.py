@@ -288,3 +288,18 @@ def test_alias_modules_are_shared():
 
     assert tilegen.quant.int8_ops is mine
     assert importlib.import_module("tilegen.comfyui.backend").BACKEND_NAME == "tilegen"
+
+
+def test_host_linear_argument_checks():
+    from tilegen_b200.streaming import int8_linear_host
+
+    x = torch.zeros(4, 256, dtype=torch.float16)
+    w = torch.zeros(8, 256, dtype=torch.int8)
+    with pytest.raises(ValueError, match="CUDA device"):
+        int8_linear_host(x, w, torch.ones(8))
+    with pytest.raises(ValueError, match="host memory"):
+        int8_linear_host(_FakeCuda(), w, torch.ones(8))
+
+
+class _FakeCuda:
+    is_cuda = True

@@ -1,0 +1,46 @@
+"""The host-buffer linear (tilegen_b200.streaming.int8_linear_host) on the GPU.
+
+Its row chunks run the same kernels as the device path on overlapping streams,
+so the output must be bit-identical to rotate+quant then the GEMM on the whole
+tensor, for ragged row counts, both input dtypes, bias and caller-given output.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from tilegen_b200 import ops
+from tilegen_b200.streaming import int8_linear_host
+from tilegen_b200.synthetic import gaussian_weight, outlier_activations
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("m,chunk", [(1, 512), (511, 512), (1300, 512), (4096, 512), (700, 64)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_host_linear_equals_device_path(cuda, m, chunk, dtype):
+    k, n = 5120, 1536
+    x = outlier_activations(m, k, seed=m, dtype=dtype)
+    w = gaussian_weight(n, k, seed=2, dtype=dtype, device=cuda)
+    wq, ws = ops.rotate_quant(w, 256)
+    bias = torch.randn(n, generator=torch.Generator().manual_seed(3)).to(cuda)
+    y = int8_linear_host(x.pin_memory(), wq, ws, bias, dtype, rows_per_chunk=chunk)
+    torch.cuda.current_stream().synchronize()
+    ref = ops.int8_gemm_dequant(*ops.rotate_quant(x.to(cuda), 256), wq, ws, bias, dtype).cpu()
+    assert not y.is_cuda and y.shape == (m, n)
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+
+
+def test_host_linear_into_caller_output_on_a_side_stream(cuda):
+    m, k, n = 2000, 13824, 5120
+    x = outlier_activations(m, k, seed=9, dtype=torch.float16).pin_memory()
+    w = gaussian_weight(n, k, seed=4, dtype=torch.float16, device=cuda)
+    wq, ws = ops.rotate_quant(w, 256)
+    out = torch.full((m, n), 7.0, dtype=torch.float32).pin_memory()
+    side = torch.cuda.Stream(device=cuda)
+    with torch.cuda.stream(side):
+        r = int8_linear_host(x, wq, ws, None, torch.float32, out=out)
+    side.synchronize()
+    assert r is out
+    ref = ops.int8_gemm_dequant(*ops.rotate_quant(x.to(cuda), 256), wq, ws, None, torch.float32).cpu()
+    assert torch.equal(out.view(torch.int32), ref.view(torch.int32))

@@ -615,7 +615,7 @@ def run_tilegen(args):
                            "traffic": QUANT_TRAFFIC_BYTES},
         "e2e": {"value": round(e2e_us, 2), "unit": "us", "h2d_bytes_per_step": x.numel() * 2,
                 "d2h_bytes_per_step": m * n * 2,
-                "path": "pinned host x -> tilegen_b200.streaming.int8_linear_host (512-row chunks: H2D, "
+                "path": "pinned host x -> tilegen_b200.streaming.int8_linear_host (chunks of 256, 512, then 1024 rows: H2D, "
                         "rotate+quant + GEMM, D2H on three streams) -> pinned host out",
                 "serial_us": round(e2e_serial_us, 2),
                 "serial_path": "one stream: H2D of x, tilegen.kernels.quantize_convrot, "

@@ -3,10 +3,11 @@
 ``int8_linear_host`` runs the same two kernels as the device path (rotate+quant,
 then the INT8 GEMM + dequant; tilegen/comfyui/backend.py:166-244 with
 ``convrot=True``) on an ``x`` that lives in pinned host memory, and writes the
-output to pinned host memory.  The rows go in chunks over three CUDA streams:
-chunk i's host->device copy, chunk i-1's kernels and chunk i-2's device->host
-copy run at the same time, so a call costs about the larger of the two PCIe
-transfers instead of their sum plus the kernels.  PCIe is full duplex, and the
+output to pinned host memory.  The rows go in chunks (growing to
+``rows_per_chunk``) over three CUDA streams: chunk i's host->device copy, chunk
+i-1's kernels and chunk i-2's device->host copy run at the same time, so a call
+costs about the larger of the two PCIe transfers instead of their sum plus the
+kernels.  PCIe is full duplex, and the
 two copy directions use separate copy engines.
 
 The call is asynchronous like a CUDA op: it returns once everything is
@@ -33,10 +34,21 @@ def _copy_streams(idx: int) -> tuple[torch.cuda.Stream, torch.cuda.Stream]:
     return s
 
 
+def _chunks(m: int, rows: int):
+    """Row ranges: a quarter chunk, a half chunk, then full chunks.  The small
+    first chunks start the device->host stream sooner (its copies are the long
+    pole); full-size chunks after that keep the per-chunk host overhead low."""
+    r0, size = 0, max(1, rows // 4)
+    while r0 < m:
+        r1 = min(r0 + size, m)
+        yield r0, r1
+        r0, size = r1, min(rows, size * 2)
+
+
 def int8_linear_host(x_host: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
                      bias: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
                      out: torch.Tensor | None = None, *, group_size: int = 256,
-                     rows_per_chunk: int = 512) -> torch.Tensor:
+                     rows_per_chunk: int = 1024) -> torch.Tensor:
     """``int8_linear(x, weight, weight_scale, bias, out_dtype, convrot=True)`` with ``x`` and
     the result in host memory.
 
@@ -75,8 +87,7 @@ def int8_linear_host(x_host: torch.Tensor, weight: torch.Tensor, weight_scale: t
         s_out.wait_stream(cur)
         with torch.cuda.stream(s_in):
             x_dev = torch.empty((m, k), dtype=x_host.dtype, device=dev)
-        for r0 in range(0, m, rows_per_chunk):
-            r1 = min(r0 + rows_per_chunk, m)
+        for r0, r1 in _chunks(m, rows_per_chunk):
             with torch.cuda.stream(s_in):
                 x_dev[r0:r1].copy_(x_host[r0:r1], non_blocking=True)
                 loaded = torch.cuda.Event()

@@ -153,22 +153,28 @@ __device__ __forceinline__ void stage2_64(float2 (&vp)[32]) {
 // Input activations (the names of backend.py's `input_act`).
 enum : int { kActNone = 0, kActGeluTanh = 1, kActGelu = 2 };
 
-// The activation in fp32, written as torch's CUDA GELU kernels evaluate it in
-// their fp32 op-math (the same expression, so the same contractions and the
-// same tanhf/erff calls):
+// The activation in fp32 on a pair, written as torch's CUDA GELU kernels
+// evaluate it in their fp32 op-math -- the same operations in the same order
+// (x_cube = (x*x)*x; inner = kBeta * fma(kKappa, x_cube, x), the contraction
+// the compiler makes of `x + kKappa * x_cube`; the same tanhf/erff calls, each
+// followed by the scalar `1 + ...`) -- with the multiplies of the two lanes
+// paired:
 //   gelu_tanh(x) = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
 //   gelu(x)      = x 0.5 (1 + erf(x / sqrt(2)))
 template <int ACT>
-__device__ __forceinline__ float act_f32(float x) {
+__device__ __forceinline__ float2 act2_f32(float2 x) {
   if (ACT == kActGeluTanh) {
     constexpr float kBeta = float(1.41421356237309504880 * 1.12837916709551257390 * 0.5);
     constexpr float kKappa = 0.044715f;
-    const float x_cube = x * x * x;
-    const float inner = kBeta * (x + kKappa * x_cube);
-    return 0.5f * x * (1.0f + tanhf(inner));
+    const float2 x_cube = mul2(mul2(x, x), x);
+    const float2 inner = mul2(make_float2(kBeta, kBeta), fma2(make_float2(kKappa, kKappa), x_cube, x));
+    const float2 one_t = make_float2(1.0f + tanhf(inner.x), 1.0f + tanhf(inner.y));
+    return mul2(mul2(make_float2(0.5f, 0.5f), x), one_t);
   } else if (ACT == kActGelu) {
     constexpr float kAlpha = float(0.70710678118654752440);
-    return x * 0.5f * (1.0f + erff(x * kAlpha));
+    const float2 xa = mul2(x, make_float2(kAlpha, kAlpha));
+    const float2 one_e = make_float2(1.0f + erff(xa.x), 1.0f + erff(xa.y));
+    return mul2(mul2(x, make_float2(0.5f, 0.5f)), one_e);
   }
   return x;
 }
@@ -203,8 +209,7 @@ __device__ __forceinline__ void unpack8(const uint4 w, float2* f) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     f[i] = unpack2_dtype<BF16>(u[i]);
-    if (ACT != kActNone)
-      f[i] = unpack2_dtype<BF16>(pack2_dtype<BF16>(make_float2(act_f32<ACT>(f[i].x), act_f32<ACT>(f[i].y))));
+    if (ACT != kActNone) f[i] = unpack2_dtype<BF16>(pack2_dtype<BF16>(act2_f32<ACT>(f[i])));
   }
 }
 

@@ -239,7 +239,7 @@ def _time_steps(fn, steps, flush, stream, marks=1):
     return [[evs[i][j].elapsed_time(evs[i][j + 1]) for j in range(marks)] for i in range(steps)]
 
 
-def _bf16_linear_us(x16, w_bf16, steps, flush, stream):
+def _bf16_linear_us(x16, w_bf16, steps, flush, stream, median=False):
     import torch
     import torch.nn.functional as F
 
@@ -253,7 +253,7 @@ def _bf16_linear_us(x16, w_bf16, steps, flush, stream):
     for _ in range(3):
         f([torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)])
     t = _time_steps(f, steps, flush, stream)
-    return statistics.mean(r[0] for r in t) * 1e3
+    return (statistics.median if median else statistics.mean)(r[0] for r in t) * 1e3
 
 
 def _int_mm_tops(dev):
@@ -275,7 +275,9 @@ def _int_mm_tops(dev):
     return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
 
 
-def _shape_table(dev, flush, stream, iters=20):
+def _shape_table(dev, flush, stream, iters=100):
+    """The four DiT projections at M = 4096 (fp16): the quantiser and the GEMM each timed
+    alone, the whole linear, and bf16 cuBLAS; medians of ``iters`` L2-flushed steps."""
     import torch
 
     from tilegen_b200 import ops
@@ -303,10 +305,10 @@ def _shape_table(dev, flush, stream, iters=20):
         for _ in range(3):
             f([torch.cuda.Event(enable_timing=True) for _ in range(3)])
         t = _time_steps(f, iters, flush, stream, marks=2)
-        tq = statistics.mean(r[0] for r in t) * 1e3
-        tg = statistics.mean(r[1] for r in t) * 1e3
-        tl = statistics.mean(r[0] for r in _time_steps(whole, iters, flush, stream)) * 1e3
-        tb = _bf16_linear_us(x, w, iters, flush, stream)
+        tq = statistics.median(r[0] for r in t) * 1e3
+        tg = statistics.median(r[1] for r in t) * 1e3
+        tl = statistics.median(r[0] for r in _time_steps(whole, iters, flush, stream)) * 1e3
+        tb = _bf16_linear_us(x, w, iters, flush, stream, median=True)
         qbytes = M_PER_RANK * k * 3 + 4 * M_PER_RANK
         rows.append({"shape": name, "K": k, "N": n, "int8_linear_us": round(tl, 2), "quant_us": round(tq, 2),
                      "gemm_us": round(tg, 2), "bf16_cublas_us": round(tb, 2), "speedup_vs_bf16": round(tb / tl, 3),

@@ -446,6 +446,69 @@ def _dit_block_bf16(dev, flush, stream, world, rank, tokens=65520, iters=10):
     return rows
 
 
+def _gather_table(dev, flush, stream, world, rank, tokens=65520, iters=10):
+    """N > 1 only: the optional all-gather of a row-sharded output (tilegen_b200.sharding.
+    gather_rows, NCCL over NVLink), outside the hot path.  o_proj's fp16 output of
+    `tokens` rows sharded over the ranks: the gather alone; then the gather and the next
+    layer (ffn_up on the local rows) back to back vs with the gather in flight while the
+    next layer runs.  Max over ranks of CUDA-event times."""
+    import torch
+    import torch.distributed as dist
+
+    from tilegen_b200 import ops
+    from tilegen_b200.sharding import gather_rows, shard_bounds
+    from tilegen_b200.synthetic import gaussian_weight
+
+    lo, hi = shard_bounds(tokens, world, rank)
+    m = hi - lo
+    y = (torch.randn(m, 5120, generator=torch.Generator(device=dev).manual_seed(rank), device=dev)
+         .to(torch.float16))
+    w = gaussian_weight(13824, 5120, seed=1, dtype=torch.float16, device=dev)
+    wq, ws = ops.rotate_quant(w, GROUP)
+    del w
+
+    def nxt():
+        return ops.int8_gemm_dequant(*ops.rotate_quant(y, GROUP), wq, ws, None, torch.float16)
+
+    def gather_only(e):
+        e[0].record(stream)
+        gather_rows(y, tokens)
+        e[1].record(stream)
+
+    def serial(e):
+        e[0].record(stream)
+        gather_rows(y, tokens)
+        nxt()
+        e[1].record(stream)
+
+    def overlapped(e):
+        e[0].record(stream)
+        pending = gather_rows(y, tokens, async_op=True)
+        nxt()
+        pending.wait()
+        e[1].record(stream)
+
+    def next_only(e):
+        e[0].record(stream)
+        nxt()
+        e[1].record(stream)
+
+    res = []
+    for fn in (gather_only, next_only, serial, overlapped):
+        for _ in range(3):
+            fn([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+        res.append(statistics.median(r[0] for r in _time_steps(fn, iters, flush, stream)) * 1e3)
+    t = torch.tensor(res, device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    g, nx, se, ov = (float(v) for v in t)
+    per = -(-tokens // world)
+    moved = (world - 1) * per * 5120 * 2  # bytes each rank receives
+    return {"tokens": tokens, "N": 5120, "dtype": "fp16", "gather_us": round(g, 1),
+            "gather_bus_gbs": round(moved / (g * 1e-6) / 1e9, 1), "next_layer": "ffn_up on the local rows",
+            "next_layer_us": round(nx, 1), "gather_then_next_us": round(se, 1),
+            "gather_overlapped_with_next_us": round(ov, 1)}
+
+
 def run_tilegen(args):
     import torch
     import torch.distributed as dist
@@ -518,8 +581,9 @@ def run_tilegen(args):
 
     # ---- end to end through the public API, host buffers, copies timed ----
     # The host-buffer linear (tilegen_b200.streaming.int8_linear_host: row chunks,
-    # H2D / kernels / D2H overlapped on three streams), and for reference the same
-    # copies and calls issued one after another on one stream.
+    # H2D / kernels / D2H overlapped on three streams, captured once and replayed
+    # as a CUDA graph), and for reference the same copies and calls issued one
+    # after another on one stream.
     from tilegen_b200.streaming import int8_linear_host
 
     x_host = x.cpu().pin_memory()
@@ -528,7 +592,7 @@ def run_tilegen(args):
 
     def e2e_step(e):
         e[0].record(stream)
-        int8_linear_host(x_host, wq, ws, None, torch.float16, out=out_host, group_size=GROUP)
+        int8_linear_host(x_host, wq, ws, None, torch.float16, out=out_host, group_size=GROUP, graph=True)
         e[1].record(stream)
 
     def e2e_serial_step(e):
@@ -571,6 +635,7 @@ def run_tilegen(args):
     if world > 1:
         dist.barrier()
     block = _dit_block_bf16(dev, flush, stream, world, rank)
+    gather = _gather_table(dev, flush, stream, world, rank) if world > 1 else None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu_us, cores, sample = _cpu_baseline_us(k, n)
         cpu = {"value": round(cpu_us, 1), "unit": "us", "cores": cores, "kind": "port", "sample": sample}
@@ -617,8 +682,9 @@ def run_tilegen(args):
                            "traffic": QUANT_TRAFFIC_BYTES},
         "e2e": {"value": round(e2e_us, 2), "unit": "us", "h2d_bytes_per_step": x.numel() * 2,
                 "d2h_bytes_per_step": m * n * 2,
-                "path": "pinned host x -> tilegen_b200.streaming.int8_linear_host (chunks of 256, 512, then 1024 rows: H2D, "
-                        "rotate+quant + GEMM, D2H on three streams) -> pinned host out",
+                "path": "pinned host x -> tilegen_b200.streaming.int8_linear_host(graph=True) (chunks of 256, 512, "
+                        "then 1024 rows: H2D, rotate+quant + GEMM, D2H on three streams, replayed as one CUDA "
+                        "graph) -> pinned host out",
                 "serial_us": round(e2e_serial_us, 2),
                 "serial_path": "one stream: H2D of x, tilegen.kernels.quantize_convrot, "
                                "tilegen.quant.int8_matmul_dequant_chunked, D2H of the output",
@@ -635,6 +701,8 @@ def run_tilegen(args):
     line["dit_block_bf16"] = {"tokens": 65520, "rows_sharded_over": world, "shapes": block}
     if sweep is not None:
         line["quant_sweep"] = {"columns": ["group", "K", "M", "dtype", "us", "GB/s", "frac_of_hbm"], "rows": sweep}
+    if gather is not None:
+        line["gather_rows"] = gather
     if act_table is not None:
         line["input_act_ffn_down"] = act_table[0]
         line["rowwise_quant"] = {"columns": ["K", "M", "dtype", "us", "GB/s", "frac_of_hbm"], "rows": act_table[1]}

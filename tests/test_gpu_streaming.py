@@ -44,3 +44,23 @@ def test_host_linear_into_caller_output_on_a_side_stream(cuda):
     assert r is out
     ref = ops.int8_gemm_dequant(*ops.rotate_quant(x.to(cuda), 256), wq, ws, None, torch.float32).cpu()
     assert torch.equal(out.view(torch.int32), ref.view(torch.int32))
+
+
+@pytest.mark.parametrize("m,k,n,chunk", [(4096, 5120, 1536, 1024), (600, 13824, 640, 128)])
+def test_host_linear_graph_replays(cuda, m, k, n, chunk):
+    """graph=True: the first call runs and captures, later calls replay on whatever the
+    same host buffers hold.  The second case sends its small chunks to the split-K
+    kernel, whose scratch the graph keeps."""
+    w = gaussian_weight(n, k, seed=5, dtype=torch.bfloat16, device=cuda)
+    wq, ws = ops.rotate_quant(w, 256)
+    bias = torch.randn(n, generator=torch.Generator().manual_seed(6)).to(cuda).half()
+    x_host = torch.empty((m, k), dtype=torch.bfloat16).pin_memory()
+    out = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+    for i in range(4):
+        x = outlier_activations(m, k, seed=10 + i, dtype=torch.bfloat16)
+        x_host.copy_(x)
+        r = int8_linear_host(x_host, wq, ws, bias, torch.bfloat16, out=out, rows_per_chunk=chunk, graph=True)
+        torch.cuda.current_stream().synchronize()
+        ref = ops.int8_gemm_dequant(*ops.rotate_quant(x.to(cuda), 256), wq, ws, bias, torch.bfloat16).cpu()
+        assert r is out
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), f"call {i}"

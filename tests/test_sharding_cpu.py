@@ -36,7 +36,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, m, fail_rank, q):
+def _worker(rank, world, port, m, fail_rank, q, overlap=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -50,9 +50,18 @@ def _worker(rank, world, port, m, fail_rank, q):
         if rank == fail_rank:
             raise RuntimeError("planted failure before the gather")
         y_local = int8_convrot_linear_local(local_rows(x, world, rank), wq, ws, None, torch.float32)
-        y = gather_rows(y_local, m)
         ref = int8_convrot_linear_local(x, wq, ws, None, torch.float32)
-        q.put((rank, "ok", bool(torch.equal(y, ref)), tuple(y.shape)))
+        if overlap:
+            # the gather in flight while the next layer runs on the local rows
+            pending = gather_rows(y_local, m, async_op=True)
+            w2 = torch.randint(-127, 128, (32, 256), dtype=torch.int8)
+            nxt = int8_convrot_linear_local(y_local.repeat(1, 4), w2, torch.rand(32) * 1e-2, None, torch.float32)
+            y = pending.wait()
+            ok = bool(torch.equal(y, ref)) and nxt.shape == (y_local.shape[0], 32) and pending.wait() is not None
+        else:
+            y = gather_rows(y_local, m)
+            ok = bool(torch.equal(y, ref))
+        q.put((rank, "ok", ok, tuple(y.shape)))
     except Exception as e:  # report, never hang
         q.put((rank, "error", type(e).__name__, str(e)[:80]))
     finally:
@@ -62,11 +71,11 @@ def _worker(rank, world, port, m, fail_rank, q):
             pass
 
 
-def _run(world, m, fail_rank=-1):
+def _run(world, m, fail_rank=-1, overlap=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, m, fail_rank, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, m, fail_rank, q, overlap)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -88,3 +97,9 @@ def test_failed_rank_surfaces_as_error_not_hang():
     res = _run(2, 16, fail_rank=1)
     assert res[1][1] == "error" and "planted" in res[1][3]
     assert res[0][1] == "error"  # the survivor's collective errors out
+
+
+def test_async_gather_overlaps_the_next_layer_gloo():
+    res = _run(2, 33, overlap=True)
+    assert [r[1] for r in res] == ["ok", "ok"], res
+    assert all(r[2] for r in res) and all(r[3] == (33, 64) for r in res)

@@ -5,7 +5,9 @@ scale are per row, the GEMM contracts over K), so N GPUs each quantise and
 multiply a contiguous block of rows against a replicated int8 weight: there is
 no collective on the path.  When a caller needs the full ``[M, N]`` output on
 every rank, ``gather_rows`` all-gathers the blocks over NCCL (NVLink), as one
-collective outside the hot path.
+collective outside the hot path; with ``async_op=True`` it returns at once and
+the caller overlaps the transfer with the next layer's kernels, waiting only
+where the gathered output is used.
 
 Blocks are ``ceil(M / world)`` rows; the last rank's block may be short or
 empty.  ``gather_rows`` pads the short blocks to the common size for the
@@ -32,8 +34,32 @@ def local_rows(x: torch.Tensor, world: int, rank: int) -> torch.Tensor:
     return x[s:e]
 
 
-def gather_rows(y_local: torch.Tensor, m_total: int, group=None) -> torch.Tensor:
-    """All-gather every rank's ``[rows_r, N]`` block into the full ``[m_total, N]``."""
+class RowGather:
+    """An all-gather of row blocks in flight (``gather_rows(..., async_op=True)``).
+
+    ``wait()`` returns the gathered ``[m_total, N]`` tensor.  On NCCL it only
+    makes the caller's current stream wait for the collective (the host does not
+    block), so kernels enqueued before ``wait()`` overlap the transfer.
+    """
+
+    def __init__(self, work, out: torch.Tensor, parts: list | None, m_total: int):
+        self._work, self._out, self._parts, self._m = work, out, parts, m_total
+
+    def wait(self) -> torch.Tensor:
+        if self._work is not None:
+            self._work.wait()
+            self._work = None
+            if self._parts is not None:
+                self._out = torch.cat(self._parts, 0)
+                self._parts = None
+        return self._out[: self._m]
+
+
+def gather_rows(y_local: torch.Tensor, m_total: int, group=None, async_op: bool = False):
+    """All-gather every rank's ``[rows_r, N]`` block into the full ``[m_total, N]``.
+
+    With ``async_op=True`` returns a ``RowGather`` whose ``wait()`` gives the result.
+    """
     world = dist.get_world_size(group)
     per = -(-m_total // world)
     n = y_local.shape[1]
@@ -42,14 +68,16 @@ def gather_rows(y_local: torch.Tensor, m_total: int, group=None) -> torch.Tensor
         buf = torch.zeros((per, n), dtype=y_local.dtype, device=y_local.device)
         buf[: y_local.shape[0]].copy_(y_local)
     buf = buf.contiguous()
+    parts = None
     if dist.get_backend(group) == "nccl":
         out = torch.empty((world * per, n), dtype=y_local.dtype, device=y_local.device)
-        dist.all_gather_into_tensor(out, buf, group=group)
+        work = dist.all_gather_into_tensor(out, buf, group=group, async_op=async_op)
     else:
         parts = [torch.empty_like(buf) for _ in range(world)]
-        dist.all_gather(parts, buf, group=group)
-        out = torch.cat(parts, 0)
-    return out[:m_total]
+        work = dist.all_gather(parts, buf, group=group, async_op=async_op)
+        out = None if async_op else torch.cat(parts, 0)
+    handle = RowGather(work if async_op else None, out, parts if async_op else None, m_total)
+    return handle if async_op else handle.wait()
 
 
 def int8_convrot_linear_local(x_local: torch.Tensor, wq: torch.Tensor, wscale: torch.Tensor,

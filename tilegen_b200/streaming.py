@@ -18,18 +18,23 @@ the same rows (the quantiser is per row and the GEMM's rows are independent).
 """
 from __future__ import annotations
 
+import threading
+from collections import OrderedDict
+
 import torch
 
 from . import ops
 
-_STREAMS: dict[int, tuple[torch.cuda.Stream, torch.cuda.Stream]] = {}
+_STREAMS: dict[int, tuple[torch.cuda.Stream, torch.cuda.Stream, torch.cuda.Stream]] = {}
 
 
-def _copy_streams(idx: int) -> tuple[torch.cuda.Stream, torch.cuda.Stream]:
+def _streams(idx: int) -> tuple[torch.cuda.Stream, torch.cuda.Stream, torch.cuda.Stream]:
+    """Per device: the host->device copy stream, the device->host copy stream and
+    the stream graphs are captured on."""
     s = _STREAMS.get(idx)
     if s is None:
         dev = torch.device("cuda", idx)
-        s = (torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev))
+        s = (torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev))
         _STREAMS[idx] = s
     return s
 
@@ -45,10 +50,45 @@ def _chunks(m: int, rows: int):
         r0, size = r1, min(rows, size * 2)
 
 
+def _enqueue(x_host, weight, weight_scale, bias, out_dtype, out, group_size, rows_per_chunk, dev, idx):
+    """Enqueue the chunked pipeline; returns the device tensors it uses, which the
+    caller keeps until its current stream has joined both copy streams (so none
+    of their memory is reused while a copy still reads it)."""
+    m, k = x_host.shape
+    cur = torch.cuda.current_stream(idx)
+    s_in, s_out, _ = _streams(idx)
+    # Both copy streams start after whatever the caller enqueued before.
+    s_in.wait_stream(cur)
+    s_out.wait_stream(cur)
+    x_dev = torch.empty((m, k), dtype=x_host.dtype, device=dev)
+    held = [x_dev]
+    for r0, r1 in _chunks(m, rows_per_chunk):
+        with torch.cuda.stream(s_in):
+            x_dev[r0:r1].copy_(x_host[r0:r1], non_blocking=True)
+            loaded = torch.cuda.Event()
+            loaded.record(s_in)
+        cur.wait_event(loaded)
+        xq, xs = ops.rotate_quant(x_dev[r0:r1], group_size)
+        y = ops.int8_gemm_dequant(xq, xs, weight, weight_scale, bias, out_dtype)
+        held += [xq, xs, y]
+        done = torch.cuda.Event()
+        done.record(cur)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done)
+            out[r0:r1].copy_(y, non_blocking=True)
+    cur.wait_stream(s_out)
+    return held
+
+
+_GRAPHS: OrderedDict = OrderedDict()
+_GRAPH_CACHE_SIZE = 4
+_GRAPH_LOCK = threading.Lock()
+
+
 def int8_linear_host(x_host: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
                      bias: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
                      out: torch.Tensor | None = None, *, group_size: int = 256,
-                     rows_per_chunk: int = 1024) -> torch.Tensor:
+                     rows_per_chunk: int = 1024, graph: bool = False) -> torch.Tensor:
     """``int8_linear(x, weight, weight_scale, bias, out_dtype, convrot=True)`` with ``x`` and
     the result in host memory.
 
@@ -56,6 +96,13 @@ def int8_linear_host(x_host: torch.Tensor, weight: torch.Tensor, weight_scale: t
     ``weight [N, K]`` int8 and ``weight_scale`` (scalar or ``[N]``) on the CUDA device
     that runs the linear; ``out`` an optional ``[M, N]`` ``out_dtype`` CPU tensor
     (pinned) to write into, else one is allocated (pinned).  Returns ``out``.
+
+    ``graph=True`` replays the whole chunked pipeline as one CUDA graph, so a call
+    costs one launch on the host instead of a few dozen API calls per chunk: the
+    first call with a given set of buffers (x_host, out, weight, scales, bias:
+    addresses, shapes and dtypes) runs eagerly and captures the graph, later calls
+    with the same buffers replay it (it reads whatever they hold then).  Up to four
+    graphs are kept, each holding its device buffers.
     """
     if x_host.is_cuda:
         raise ValueError("int8_linear_host: x_host must be in host memory (use int8_linear for CUDA tensors)")
@@ -76,31 +123,45 @@ def int8_linear_host(x_host: torch.Tensor, weight: torch.Tensor, weight_scale: t
         raise ValueError(f"int8_linear_host: out must be a contiguous host [{m}, {n}] {out_dtype} tensor")
     if m == 0:
         return out
+    if graph and not x_host.is_contiguous():
+        raise ValueError("int8_linear_host: graph=True needs a contiguous x_host (its address is captured)")
     x_host = x_host.contiguous()
     dev = weight.device
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    args = (x_host, weight, weight_scale, bias, out_dtype, out, group_size, rows_per_chunk, dev, idx)
     with torch.cuda.device(idx):
+        if not graph:
+            _enqueue(*args)
+            return out
+        key = (idx, x_host.data_ptr(), tuple(x_host.shape), x_host.dtype, out.data_ptr(), out_dtype,
+               weight.data_ptr(), tuple(weight.shape), weight_scale.data_ptr(), weight_scale.numel(),
+               weight_scale.dtype, weight_scale.device, None if bias is None else
+               (bias.data_ptr(), bias.numel(), bias.dtype, bias.device), group_size, rows_per_chunk)
+        with _GRAPH_LOCK:
+            entry = _GRAPHS.get(key)
+            if entry is not None:
+                _GRAPHS.move_to_end(key)
+        if entry is not None:
+            entry[0].replay()
+            return out
+        # First call: run it eagerly on the capture stream (one-time launch
+        # set-up, and any split-K scratch, which is cached per stream, is made
+        # and zeroed outside the capture), then capture the same sequence there.
         cur = torch.cuda.current_stream(idx)
-        s_in, s_out = _copy_streams(idx)
-        # Both copy streams start after whatever the caller enqueued before.
-        s_in.wait_stream(cur)
-        s_out.wait_stream(cur)
-        with torch.cuda.stream(s_in):
-            x_dev = torch.empty((m, k), dtype=x_host.dtype, device=dev)
-        for r0, r1 in _chunks(m, rows_per_chunk):
-            with torch.cuda.stream(s_in):
-                x_dev[r0:r1].copy_(x_host[r0:r1], non_blocking=True)
-                loaded = torch.cuda.Event()
-                loaded.record(s_in)
-            cur.wait_event(loaded)
-            xq, xs = ops.rotate_quant(x_dev[r0:r1], group_size)
-            y = ops.int8_gemm_dequant(xq, xs, weight, weight_scale, bias, out_dtype)
-            done = torch.cuda.Event()
-            done.record(cur)
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(done)
-                out[r0:r1].copy_(y, non_blocking=True)
-            y.record_stream(s_out)  # the allocator keeps y until its copy has run
-        x_dev.record_stream(cur)
-        cur.wait_stream(s_out)
+        cap = _streams(idx)[2]
+        cap.wait_stream(cur)
+        with torch.cuda.stream(cap):
+            _enqueue(*args)
+        cur.wait_stream(cap)
+        torch.cuda.synchronize(idx)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            held = _enqueue(*args)
+        scratch = ops._SPLITK_WS.get((idx, cap.cuda_stream))
+        if scratch is not None:
+            held.append(scratch)  # the graph's kernels use this very buffer
+        with _GRAPH_LOCK:
+            _GRAPHS[key] = (g, held)
+            while len(_GRAPHS) > _GRAPH_CACHE_SIZE:
+                _GRAPHS.popitem(last=False)
     return out

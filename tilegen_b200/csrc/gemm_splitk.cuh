@@ -96,6 +96,13 @@ __global__ void __launch_bounds__(splitk::THREADS, 1)
   if (threadIdx.x == 0) {
     prefetch_tmap(&tma_w);
     prefetch_tmap(&tma_x);
+    // The weight stream is this kernel's whole cost at small M and does not
+    // depend on the kernel before it: pull this CTA's slice of W into L2 now,
+    // while that kernel (the activation quantiser) may still be running, so
+    // the loads after the programmatic-dependent wait hit L2.  Only into L2:
+    // the weights may have been written by the kernel before, so nothing lands
+    // in shared memory until that wait.
+    for (int kb = kb0; kb < kb1; ++kb) tma_prefetch_l2_2d(&tma_w, kb * BK, n0);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);

@@ -313,3 +313,15 @@ def test_small_m_routing_boundaries():
     assert splitk_route(64, 5120, 5120) and not splitk_route(65, 5120, 5120)        # o_proj
     assert splitk_route(128, 5120, 13824) and not splitk_route(129, 5120, 13824)    # ffn_down
     assert not splitk_route(0, 5120, 5120) and not splitk_route(4096, 5120, 5120)
+
+
+def test_host_linear_chunk_schedule_covers_rows():
+    from tilegen_b200.streaming import _chunks
+
+    for m in (1, 7, 255, 256, 1000, 4096, 65520):
+        for rows in (1, 3, 64, 512, 1024):
+            ch = list(_chunks(m, rows))
+            assert ch[0][0] == 0 and ch[-1][1] == m
+            assert all(a[1] == b[0] and a[0] < a[1] for a, b in zip(ch, ch[1:] + [(m, m + 1)]))
+            sizes = [b - a for a, b in ch]
+            assert max(sizes) <= rows and sizes[0] == min(max(1, rows // 4), m)

@@ -79,13 +79,11 @@ template <int NST, bool BF16, int ACT>
 int launch_rotquant_t(const CUtensorMap& tm, const tg::RotQuantParams& p, int threads, uint32_t smem, int dev,
                       int sms, cudaStream_t st) {
   static uint32_t attr_done[kMaxDevices];
-  static int occ_cache[kMaxDevices][4][2];  // [dev][stages-1..][threads>256]
   auto kern = tg::rotquant_kernel<NST, BF16, ACT>;
   if (!ensure_smem_attr(kern, dev, smem, attr_done)) return TG_ERR_CUDA;
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem) != cudaSuccess || occ < 1)
     return TG_ERR_CUDA;
-  (void)occ_cache;
   const int64_t grid64 = std::min<int64_t>(p.nbatches, int64_t(sms) * occ);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

@@ -120,8 +120,11 @@ int tg_int8_gemm_dequant(const int8_t *xq, const float *xscale, const int8_t *wq
  * and preview steps), bit-identical to tg_int8_gemm_dequant.  Also replaces
  * `int8_matmul_dequant_chunked` (tilegen/quant/int8_ops.py:22-70), whose GEMM
  * at small M is whatever torch._int_mm does.  The weight streams through all
- * SMs: K is split across CTAs, each adds its exact int32 partial sums into a
- * scratch accumulator, and the last CTA of each 128-column tile dequantises.
+ * SMs: K is split across the CTAs of each 128-column tile, whose exact int32
+ * partial sums are added either in shared memory (the tile's CTAs run as one
+ * thread-block cluster: K split at most 8 ways; the workspace is then not
+ * touched) or in the workspace, where the last CTA of the tile dequantises
+ * (tg_int8_gemm_dequant_splitk_config tells which).
  *
  * Arguments as tg_int8_gemm_dequant (M > 128 gives TG_ERR_UNSUPPORTED), plus:
  *   workspace  tg_int8_gemm_dequant_splitk_workspace(M, N) bytes, 256-byte
@@ -140,6 +143,16 @@ size_t tg_int8_gemm_dequant_splitk_workspace(int64_t M, int64_t N);
 
 /* Largest M tg_int8_gemm_dequant_splitk accepts (128). */
 int64_t tg_int8_gemm_dequant_splitk_max_m(void);
+
+/*
+ * How tg_int8_gemm_dequant_splitk runs an M x N x K problem with this output
+ * dtype and bias presence on the current device: *slices = CTAs that split the
+ * K of each 128-column tile; *cluster = 1 when they run as one thread-block
+ * cluster and reduce in shared memory, 0 when they reduce through the
+ * workspace.  No reference counterpart (for tests and tuning).
+ */
+int tg_int8_gemm_dequant_splitk_config(int64_t M, int64_t N, int64_t K, int out_dtype, int has_bias, int *slices,
+                                       int *cluster);
 
 /*
  * tg_int8_gemm_dequant_splitk for callers that cannot allocate device memory:

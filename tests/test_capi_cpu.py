@@ -121,3 +121,13 @@ def test_quantize_act_checks_before_device_work():
     # tg_rotate_quant keeps rejecting group 1 (the row-wise branch is tg_quantize_act's)
     assert L.tg_rotate_quant(p, _lib.TG_DT_F16, 4, 320, 1, p, p, None) == _lib.TG_ERR_UNSUPPORTED
     assert L.tg_rotate_quant(p, _lib.TG_DT_F16, -1, 320, 1, p, p, None) == _lib.TG_ERR_INVALID_ARG
+
+
+def test_splitk_config_checks_arguments():
+    L = _lib.lib()
+    sl, cl = ctypes.c_int(0), ctypes.c_int(0)
+    assert "tg_int8_gemm_dequant_splitk_config" in _lib.declared_functions()
+    for args in ((0, 64, 64, 1, 0), (129, 64, 64, 1, 0), (4, 0, 64, 1, 0), (4, 64, 0, 1, 0), (4, 64, 64, 9, 0)):
+        assert L.tg_int8_gemm_dequant_splitk_config(*args, ctypes.byref(sl), ctypes.byref(cl)) == \
+            _lib.TG_ERR_INVALID_ARG
+    assert L.tg_int8_gemm_dequant_splitk_config(4, 64, 64, 1, 0, None, None) == _lib.TG_ERR_INVALID_ARG

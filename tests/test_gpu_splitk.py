@@ -56,9 +56,17 @@ def _healthy_device(cuda):
     assert _lib.device_status(0) == 0, "a bounded wait expired during the test"
 
 
+# (n, k, cluster): 1536 x 2048 splits K 16 ways (partials reduced through the
+# workspace); 5120 x 2048 splits it 6 ways (one cluster per column tile,
+# reduced in shared memory).
+FORMS = [(1536, 2048, 0), (5120, 2048, 1)]
+
+
+@pytest.mark.parametrize("n,k,cluster", FORMS)
 @pytest.mark.parametrize("m", [1, 2, 7, 16, 17, 31, 32, 33, 48, 63, 64, 65, 96, 100, 127, 128])
-def test_rows_bit_exact_vs_tiled_kernel(cuda, m):
-    case = _case(m, 1536, 2048, seed=m)
+def test_rows_bit_exact_vs_tiled_kernel(cuda, m, n, k, cluster):
+    assert _lib.splitk_config(m, n, k)[1] == cluster
+    case = _case(m, n, k, seed=m)
     a = _run(case, torch.float16, cuda, 128)
     b = _run(case, torch.float16, cuda, 0)
     assert np.array_equal(_bits(a), _bits(b))
@@ -67,8 +75,11 @@ def test_rows_bit_exact_vs_tiled_kernel(cuda, m):
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("bias_dtype", [None, torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("scalar_ws", [False, True])
-def test_against_oracle(cuda, out_dtype, bias_dtype, scalar_ws):
-    m, n, k = 24, 640, 1152
+@pytest.mark.parametrize("n,cluster", [(640, 0), (4096, 1)])
+def test_against_oracle(cuda, out_dtype, bias_dtype, scalar_ws, n, cluster):
+    m, k = 24, 1152
+    code = {torch.float32: _lib.TG_DT_F32, torch.float16: _lib.TG_DT_F16, torch.bfloat16: _lib.TG_DT_BF16}[out_dtype]
+    assert _lib.splitk_config(m, n, k, code, bias_dtype is not None)[1] == cluster
     case = _case(m, n, k, seed=3, scalar_ws=scalar_ws, bias_dtype=bias_dtype)
     y = _run(case, out_dtype, cuda, 128)
     xq, xs, wq, ws, bias = case
@@ -83,6 +94,8 @@ def test_against_oracle(cuda, out_dtype, bias_dtype, scalar_ws):
 
 @pytest.mark.parametrize("n,k", [(8, 16), (136, 144), (1000, 4112), (5120, 13824), (15360, 5120)])
 def test_ragged_and_dit_shapes(cuda, n, k):
+    if n >= 5120:  # the DiT shapes reduce in shared memory
+        assert all(_lib.splitk_config(m, n, k)[1] == 1 for m in (1, 64, 128))
     for m in (1, 64, 128):
         case = _case(m, n, k, seed=n + k + m)
         a = _run(case, torch.bfloat16, cuda, 128)

@@ -114,6 +114,9 @@ def lib() -> ctypes.CDLL:
         L.tg_int8_gemm_dequant_splitk_workspace.argtypes = [i64, i64]
         L.tg_int8_gemm_dequant_splitk_workspace.restype = ctypes.c_size_t
         L.tg_int8_gemm_dequant_splitk_max_m.restype = i64
+        L.tg_int8_gemm_dequant_splitk_config.argtypes = [i64, i64, i64, i32, i32, ctypes.POINTER(i32),
+                                                         ctypes.POINTER(i32)]
+        L.tg_int8_gemm_dequant_splitk_config.restype = i32
         _lib = L
     return _lib
 
@@ -124,6 +127,15 @@ def check(func: str, status: int) -> None:
         if status in (TG_ERR_INVALID_ARG, TG_ERR_UNSUPPORTED, TG_ERR_MISALIGNED):
             raise ValueError(f"{func}: {msg} (status {status})")
         raise TileGenError(func, status, msg)
+
+
+def splitk_config(m: int, n: int, k: int, out_dtype_code: int = TG_DT_F16, has_bias: bool = False) -> tuple[int, int]:
+    """(slices, cluster flag) of the small-M kernel for an m x n x k problem on the current device."""
+    sl, cl = ctypes.c_int(0), ctypes.c_int(0)
+    check("tg_int8_gemm_dequant_splitk_config",
+          lib().tg_int8_gemm_dequant_splitk_config(int(m), int(n), int(k), int(out_dtype_code), int(has_bias),
+                                                   ctypes.byref(sl), ctypes.byref(cl)))
+    return sl.value, cl.value
 
 
 def gemm_config(m: int, n: int) -> tuple[int, int]:

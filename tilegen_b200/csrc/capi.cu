@@ -503,22 +503,68 @@ SplitKWs splitk_ws(int64_t M, int64_t N) {
   return w;
 }
 
+// Whether the cluster form of the split-K kernel runs with `slices` CTAs per
+// cluster on device `dev`: at most 8, and the occupancy calculator schedules at
+// least one such cluster (cached per device and size).
+template <int MPAD, int OUT, bool HAS_BIAS>
+bool splitk_cluster_ok(int slices, int dev) {
+  static uint32_t attr_done[kMaxDevices];
+  static uint8_t ok_cache[kMaxDevices][9];  // 0 unknown, 1 yes, 2 no
+  if (slices < 1 || slices > 8) return false;
+  constexpr uint32_t smem = tg::splitk::smem_bytes(MPAD);
+  auto kcl = tg::gemm_i8_splitk_kernel<MPAD, OUT, HAS_BIAS, true>;
+  if (!ensure_smem_attr(kcl, dev, smem, attr_done)) {
+    cudaGetLastError();
+    return false;
+  }
+  uint8_t& ok = ok_cache[dev][slices];
+  if (ok == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(unsigned(slices), 1);
+    cfg.blockDim = dim3(tg::splitk::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(slices);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    ok = (cudaOccupancyMaxActiveClusters(&n, kcl, &cfg) == cudaSuccess && n > 0) ? 1 : 2;
+    cudaGetLastError();  // a refusal here only selects the other form
+  }
+  return ok == 1;
+}
+
 template <int MPAD, int OUT, bool HAS_BIAS>
 int launch_splitk_t(const CUtensorMap& tw, const CUtensorMap& tx, const tg::SplitKParams& p, int tiles, int dev,
                     cudaStream_t st) {
   static uint32_t attr_done[kMaxDevices];
   constexpr uint32_t smem = tg::splitk::smem_bytes(MPAD);
-  auto kern = tg::gemm_i8_splitk_kernel<MPAD, OUT, HAS_BIAS>;
-  if (!ensure_smem_attr(kern, dev, smem, attr_done)) return TG_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.gridDim = dim3(unsigned(p.slices), unsigned(tiles));
   cfg.blockDim = dim3(tg::splitk::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = unsigned(p.slices);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
+  // The slices of a column tile as one cluster, reduced in shared memory,
+  // when K is split at most 8 ways and such a cluster fits on the device.
+  if (splitk_cluster_ok<MPAD, OUT, HAS_BIAS>(p.slices, dev)) {
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, tg::gemm_i8_splitk_kernel<MPAD, OUT, HAS_BIAS, true>, tw, tx, p) != cudaSuccess)
+      return TG_ERR_CUDA;
+    return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
+  }
+  auto kern = tg::gemm_i8_splitk_kernel<MPAD, OUT, HAS_BIAS, false>;
+  if (!ensure_smem_attr(kern, dev, smem, attr_done)) return TG_ERR_CUDA;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, tw, tx, p) != cudaSuccess) return TG_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
@@ -537,6 +583,20 @@ int launch_splitk_m(const CUtensorMap& tw, const CUtensorMap& tx, const tg::Spli
   }
 }
 
+// K split of the small-M GEMM: about 1.6 CTAs per SM stream the weight
+// (measured at M=1 on the DiT shapes: more in flight costs DRAM efficiency,
+// fewer leaves bandwidth unused), so K is split until tiles x slices is nearest
+// that, every slice non-empty.  Returns the slice count; *kb_per = k-blocks each.
+int splitk_slices(int64_t N, int64_t K, int sms, int* kb_per) {
+  using namespace tg::splitk;
+  const int tiles = int((N + BNW - 1) / BNW);
+  const int k_blocks = int((K + BK - 1) / BK);
+  int slices = (16 * sms / 10 + tiles / 2) / tiles;
+  slices = slices < 1 ? 1 : (slices > k_blocks ? k_blocks : slices);
+  *kb_per = (k_blocks + slices - 1) / slices;
+  return (k_blocks + *kb_per - 1) / *kb_per;
+}
+
 // The split-K launch over a zero-initialised scratch (count, acc), shared by
 // the workspace entry point and any other caller that owns such scratch.
 int splitk_launch(const int8_t* xq, const float* xscale, const int8_t* wq, const float* wscale,
@@ -549,13 +609,8 @@ int splitk_launch(const int8_t* xq, const float* xscale, const int8_t* wq, const
   const int mpad = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
   const int tiles = int((N + BNW - 1) / BNW);
   const int k_blocks = int((K + BK - 1) / BK);
-  // About 1.6 CTAs per SM stream the weight (measured at M=1 on the DiT
-  // shapes: more in flight costs DRAM efficiency, fewer leaves bandwidth
-  // unused): split K until tiles x slices is nearest that, every slice non-empty.
-  int slices = (16 * info.sms / 10 + tiles / 2) / tiles;
-  slices = slices < 1 ? 1 : (slices > k_blocks ? k_blocks : slices);
-  const int kb_per = (k_blocks + slices - 1) / slices;
-  slices = (k_blocks + kb_per - 1) / kb_per;
+  int kb_per;
+  const int slices = splitk_slices(N, K, info.sms, &kb_per);
 
   CUtensorMap tw, tx;
   if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, uint64_t(K), uint64_t(N), uint64_t(K), BK, BNW,
@@ -615,6 +670,27 @@ int tg_int8_gemm_dequant_splitk(const int8_t* xq, const float* xscale, const int
 }
 
 int64_t tg_int8_gemm_dequant_splitk_max_m(void) { return tg::splitk::M_MAX; }
+
+int tg_int8_gemm_dequant_splitk_config(int64_t M, int64_t N, int64_t K, int out_dtype, int has_bias, int* slices,
+                                       int* cluster) {
+  if (M < 1 || M > tg::splitk::M_MAX || N < 1 || K < 1 || !slices || !cluster) return TG_ERR_INVALID_ARG;
+  if (out_dtype != TG_DT_F32 && out_dtype != TG_DT_F16 && out_dtype != TG_DT_BF16) return TG_ERR_INVALID_ARG;
+  int dev;
+  DeviceInfo info;
+  if (!current_device(&dev, &info)) return TG_ERR_CUDA;
+  int kb_per;
+  const int s = splitk_slices(N, K, info.sms, &kb_per);
+  const int mpad = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
+  const bool hb = has_bias != 0;
+#define TG_SK_OK(MP, O) (hb ? splitk_cluster_ok<MP, O, true>(s, dev) : splitk_cluster_ok<MP, O, false>(s, dev))
+#define TG_SK_OUT(MP) (out_dtype == TG_DT_F32 ? TG_SK_OK(MP, 0) : out_dtype == TG_DT_F16 ? TG_SK_OK(MP, 1) : TG_SK_OK(MP, 2))
+  const bool cl = mpad == 16 ? TG_SK_OUT(16) : mpad == 32 ? TG_SK_OUT(32) : mpad == 64 ? TG_SK_OUT(64) : TG_SK_OUT(128);
+#undef TG_SK_OUT
+#undef TG_SK_OK
+  *slices = s;
+  *cluster = cl ? 1 : 0;
+  return TG_OK;
+}
 
 }  // extern "C"
 

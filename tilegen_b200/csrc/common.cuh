@@ -238,7 +238,14 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   return r;
 }
 
-// All threads of both CTAs of the cluster; release/acquire orders the shared
+// 32-bit load from another CTA's shared memory (a shared::cluster address).
+__device__ __forceinline__ int32_t ld_shared_cluster_s32(uint32_t cluster_addr) {
+  int32_t v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
+// All threads of every CTA of the cluster; release/acquire orders the shared
 // memory accesses (and mbarrier initialisation) made before it.
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");

@@ -13,13 +13,20 @@
 //  * K is split: CTA (s, t) multiplies column tile t over k-blocks
 //    [s*kb_per_slice, ...), so that N/128 x slices CTAs stream the weight
 //    from all SMs.
-//  * Each CTA adds its int32 partial tile into an [M, N] int32 scratch
-//    accumulator with red.global.add (integer addition: exact and
-//    order-independent), then counts itself in count[t].  The CTA that brings
-//    count[t] to `slices` reads the finished sums, applies the dequantisation
-//    (one rounding per operation, as the reference), stores the output, and
-//    writes zeros back over its accumulator tile and counter.  The scratch is
-//    therefore all-zero between launches; it must be zero before the first.
+//  * The partial tiles are summed in one of two ways (integer addition: exact
+//    and order-independent either way), then dequantised with one rounding
+//    per operation, as the reference:
+//    - CL (K split at most 8 ways): the slices of a column tile are one
+//      thread-block cluster.  Each CTA puts its partial tile in its own shared
+//      memory (the finished operand ring); after a cluster barrier, CTA r
+//      sums rows r, r + slices, ... from all of them over distributed shared
+//      memory and stores them.  No scratch in global memory.
+//    - otherwise each CTA adds its partial into an [M, N] int32 scratch
+//      accumulator with red.global.add, then counts itself in count[t]; the
+//      CTA that brings count[t] to `slices` reads the finished sums, stores
+//      the output and writes zeros back over its accumulator tile and
+//      counter.  That scratch is all-zero between launches (zero before the
+//      first).
 // Roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
 // warps 2-5 epilogue.  Every wait is bounded (common.cuh).
 #pragma once
@@ -58,8 +65,22 @@ struct SplitKParams {
   void* out;         // [M, N] of OUT
 };
 
-// MPAD: activation rows padded to 16, 32, 64 or 128 (the UMMA N); OUT: tg_dtype.
-template <int MPAD, int OUT, bool HAS_BIAS>
+// out = ((float(acc) * xs) * ws) + bias, one rounding per operation (no FMA),
+// stored as OUT with round-to-nearest-even.
+template <int OUT, bool HAS_BIAS>
+__device__ __forceinline__ void store_dequant(char* o, int32_t acc, float xs, float ws, float bs) {
+  float r = __int2float_rn(acc);
+  r = __fmul_rn(r, xs);
+  r = __fmul_rn(r, ws);
+  if (HAS_BIAS) r = __fadd_rn(r, bs);
+  if (OUT == 0) *reinterpret_cast<float*>(o) = r;
+  else if (OUT == 1) *reinterpret_cast<__half*>(o) = __float2half_rn(r);
+  else *reinterpret_cast<__nv_bfloat16*>(o) = __float2bfloat16_rn(r);
+}
+
+// MPAD: activation rows padded to 16, 32, 64 or 128 (the UMMA N); OUT: tg_dtype;
+// CL: launched with clusters of gridDim.x CTAs (all slices of a column tile).
+template <int MPAD, int OUT, bool HAS_BIAS, bool CL>
 __global__ void __launch_bounds__(splitk::THREADS, 1)
     gemm_i8_splitk_kernel(const __grid_constant__ CUtensorMap tma_w, const __grid_constant__ CUtensorMap tma_x,
                           const SplitKParams p) {
@@ -191,7 +212,23 @@ __global__ void __launch_bounds__(splitk::THREADS, 1)
     const int n = n0 + quarter * 32 + lane;
     // Warp-uniform: tcgen05.ld below is executed by all 32 lanes or none.
     const bool got = __all_sync(0xffffffffu, wait(&tfull_bar, 0u, DEVERR_MMA_TIMEOUT));
-    if (got) {
+    if (CL) {
+      // The partial tile into this CTA's operand ring, which every MMA has
+      // finished reading once tfull completed: P[m][nl], 128 int32 per row m,
+      // consecutive lanes at consecutive words.
+      int32_t* P = reinterpret_cast<int32_t*>(smem) + quarter * 32 + lane;
+      if (got) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int h = 0; h < MPAD; h += 16) {
+          uint32_t v[16];
+          tmem_ld_32x32b_x16(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(h), v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) P[(h + j) * BNW] = static_cast<int32_t>(v[j]);
+        }
+      }
+    } else if (got) {
       tc_fence_after();
       // 16 columns (activation rows) at a time; coalesced over the warp: 32
       // consecutive n of one row m per add.
@@ -211,13 +248,15 @@ __global__ void __launch_bounds__(splitk::THREADS, 1)
       }
       __threadfence();
     }
-    named_barrier(1, 128);
-    // Counted even after a wait gave up (that slice then adds nothing), so
-    // the last slice still returns the scratch to zero; the status word
-    // reports the failure.
-    if (et == 0) last_slice = atomicAdd(p.count + tile, 1u) == uint32_t(p.slices - 1);
-    named_barrier(1, 128);
-    if (last_slice) {
+    if (!CL) {
+      named_barrier(1, 128);
+      // Counted even after a wait gave up (that slice then adds nothing), so
+      // the last slice still returns the scratch to zero; the status word
+      // reports the failure.
+      if (et == 0) last_slice = atomicAdd(p.count + tile, 1u) == uint32_t(p.slices - 1);
+      named_barrier(1, 128);
+    }
+    if (!CL && last_slice) {
       // Every slice's additions are in: dequantise this column tile and put
       // the accumulator and the counter back to zero.
       __threadfence();
@@ -251,13 +290,7 @@ __global__ void __launch_bounds__(splitk::THREADS, 1)
           for (int j = 0; j < RB; ++j, zp += stride, o += ostride) {
             if (m0 + j < p.M) {
               __stcg(zp, 0);
-              float r = __int2float_rn(a[j]);
-              r = __fmul_rn(r, __ldg(p.xscale + m0 + j));
-              r = __fmul_rn(r, ws);
-              if (HAS_BIAS) r = __fadd_rn(r, bs);
-              if (OUT == 0) *reinterpret_cast<float*>(o) = r;
-              else if (OUT == 1) *reinterpret_cast<__half*>(o) = __float2half_rn(r);
-              else *reinterpret_cast<__nv_bfloat16*>(o) = __float2bfloat16_rn(r);
+              store_dequant<OUT, HAS_BIAS>(o, a[j], __ldg(p.xscale + m0 + j), ws, bs);
             }
           }
           arow += RB * stride;
@@ -267,6 +300,61 @@ __global__ void __launch_bounds__(splitk::THREADS, 1)
       named_barrier(1, 128);
       if (et == 0) p.count[tile] = 0u;
     }
+  }
+
+  if (CL) {
+    // Every CTA of the cluster reaches both barriers, also after a wait gave
+    // up (its sums are then wrong, and the status word says so); the barriers
+    // are warp-aligned, so each warp reconverges first.
+    __syncwarp();
+    cluster_sync();  // all partial tiles are in place
+    if (warp >= 2) {
+      const int nl = (warp & 3) * 32 + lane;
+      const int n = n0 + nl;
+      if (n < p.N) {
+        const float ws = p.wscale[p.wscale_bcast ? 0 : n];
+        float bs = 0.0f;
+        if (HAS_BIAS) {
+          if (p.bias_dtype == TG_DT_F32) bs = static_cast<const float*>(p.bias)[n];
+          else if (p.bias_dtype == TG_DT_F16) bs = __half2float(static_cast<const __half*>(p.bias)[n]);
+          else bs = __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n]);
+        }
+        const int S = p.slices;  // 1..8
+        // This lane's column of P in every CTA of the cluster (a CTA's window
+        // is contiguous, so row m is at + m * 512 bytes).
+        uint32_t peer[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          peer[q] = mapa_shared(smem_u32(smem) + uint32_t(nl) * 4u, uint32_t(q < S ? q : 0));
+        char* o = static_cast<char*>(p.out) + size_t(n) * (OUT == 0 ? 4 : 2);
+        const size_t ostride = size_t(p.N) * (OUT == 0 ? 4 : 2);
+        // Rows rank, rank + S, ...: four rows' loads (up to 32) in flight at
+        // once, so the distributed-shared-memory latencies overlap.
+#pragma unroll 1
+        for (int m = int(cluster_ctarank()); m < p.M; m += 4 * S) {
+          int32_t part[4][8];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int mm = m + r * S;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              part[r][q] = (q < S && mm < p.M) ? ld_shared_cluster_s32(peer[q] + uint32_t(mm * BNW) * 4u) : 0;
+          }
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int mm = m + r * S;
+            if (mm < p.M) {
+              int32_t sum = 0;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) sum += part[r][q];
+              store_dequant<OUT, HAS_BIAS>(o + size_t(mm) * ostride, sum, __ldg(p.xscale + mm), ws, bs);
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+    cluster_sync();  // no CTA leaves while another still reads its shared memory
   }
 
   __syncwarp();

@@ -310,7 +310,8 @@ def test_small_m_routing_boundaries():
 
     assert SPLITK_MAX_M == 128
     assert splitk_route(24, 15360, 5120) and not splitk_route(25, 15360, 5120)      # qkv
-    assert splitk_route(64, 5120, 5120) and not splitk_route(65, 5120, 5120)        # o_proj
+    assert splitk_route(128, 5120, 5120) and not splitk_route(129, 5120, 5120)      # o_proj
+    assert splitk_route(24, 13824, 5120) and not splitk_route(32, 13824, 5120)      # ffn_up
     assert splitk_route(128, 5120, 13824) and not splitk_route(129, 5120, 13824)    # ffn_down
     assert not splitk_route(0, 5120, 5120) and not splitk_route(4096, 5120, 5120)
 

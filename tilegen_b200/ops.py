@@ -173,12 +173,11 @@ def splitk_route(m: int, n: int, k: int) -> bool:
     Measured on B200 at the DiT shapes against the tiled kernel (whose M <= 128
     tiles give only N/128 CTAs), whole linears replayed from a CUDA graph with
     L2 flushed before each (cold weights, as in a model): split-K is faster for
-    M <= 24 everywhere, up to 64 rows when N <= 8192, and up to 128 rows when
-    K >= 8192.
+    M <= 24 everywhere, and up to 128 rows when N <= 8192 or K >= 8192.
     """
     if not 0 < m <= SPLITK_MAX_M:
         return False
-    return m <= 24 or (m <= 64 and n <= 8192) or (m <= 128 and k >= 8192)
+    return m <= 24 or n <= 8192 or k >= 8192
 
 
 # Split-K scratch, one per (device, stream): zero-filled when created and left

@@ -239,7 +239,7 @@ def _time_steps(fn, steps, flush, stream, marks=1):
     return [[evs[i][j].elapsed_time(evs[i][j + 1]) for j in range(marks)] for i in range(steps)]
 
 
-def _bf16_linear_us(x16, w_bf16, steps, flush, stream, median=False):
+def _bf16_linear_us(x16, w_bf16, steps, flush, stream):
     import torch
     import torch.nn.functional as F
 
@@ -253,7 +253,7 @@ def _bf16_linear_us(x16, w_bf16, steps, flush, stream, median=False):
     for _ in range(3):
         f([torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)])
     t = _time_steps(f, steps, flush, stream)
-    return (statistics.median if median else statistics.mean)(r[0] for r in t) * 1e3
+    return statistics.mean(r[0] for r in t) * 1e3
 
 
 def _int_mm_tops(dev):
@@ -277,8 +277,11 @@ def _int_mm_tops(dev):
 
 def _shape_table(dev, flush, stream, iters=100):
     """The four DiT projections at M = 4096 (fp16): the quantiser and the GEMM each timed
-    alone, the whole linear, and bf16 cuBLAS; medians of ``iters`` L2-flushed steps."""
+    alone, the whole linear, and bf16 cuBLAS; medians of ``iters`` L2-flushed steps of
+    each, the three kinds of step interleaved so that all see the same clock and power
+    state (seconds of sustained load pull the clock below its maximum)."""
     import torch
+    import torch.nn.functional as F
 
     from tilegen_b200 import ops
     from tilegen_b200.synthetic import DIT_SHAPES, dit_activations, gaussian_weight
@@ -288,8 +291,9 @@ def _shape_table(dev, flush, stream, iters=100):
         x = dit_activations(name, M_PER_RANK, seed=0, dtype=torch.float16, device=dev)
         w = gaussian_weight(n, k, seed=1, dtype=torch.bfloat16, device=dev)
         wq, ws = ops.rotate_quant(w, GROUP)
+        xb = x.to(torch.bfloat16)
 
-        def f(e):
+        def split(e):
             e[0].record(stream)
             xq, xs = ops.rotate_quant(x, GROUP)
             e[1].record(stream)
@@ -302,19 +306,32 @@ def _shape_table(dev, flush, stream, iters=100):
             ops.int8_gemm_dequant(xq, xs, wq, ws, None, torch.float16)
             e[1].record(stream)
 
-        for _ in range(3):
-            f([torch.cuda.Event(enable_timing=True) for _ in range(3)])
-        t = _time_steps(f, iters, flush, stream, marks=2)
-        tq = statistics.median(r[0] for r in t) * 1e3
-        tg = statistics.median(r[1] for r in t) * 1e3
-        tl = statistics.median(r[0] for r in _time_steps(whole, iters, flush, stream)) * 1e3
-        tb = _bf16_linear_us(x, w, iters, flush, stream, median=True)
+        def bf16(e):
+            e[0].record(stream)
+            F.linear(xb, w)
+            e[1].record(stream)
+
+        kinds = ((split, 3), (whole, 2), (bf16, 2))
+        for fn, marks in kinds:
+            for _ in range(3):
+                fn([torch.cuda.Event(enable_timing=True) for _ in range(marks)])
+        evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(marks)] for _ in range(iters)]
+               for _, marks in kinds]
+        for i in range(iters):
+            for j, (fn, _) in enumerate(kinds):
+                flush.zero_()
+                fn(evs[j][i])
+        torch.cuda.synchronize()
+        tq = statistics.median(e[0].elapsed_time(e[1]) for e in evs[0]) * 1e3
+        tg = statistics.median(e[1].elapsed_time(e[2]) for e in evs[0]) * 1e3
+        tl = statistics.median(e[0].elapsed_time(e[1]) for e in evs[1]) * 1e3
+        tb = statistics.median(e[0].elapsed_time(e[1]) for e in evs[2]) * 1e3
         qbytes = M_PER_RANK * k * 3 + 4 * M_PER_RANK
         rows.append({"shape": name, "K": k, "N": n, "int8_linear_us": round(tl, 2), "quant_us": round(tq, 2),
                      "gemm_us": round(tg, 2), "bf16_cublas_us": round(tb, 2), "speedup_vs_bf16": round(tb / tl, 3),
                      "quant_gbs": round(qbytes / (tq * 1e-6) / 1e9, 1),
                      "gemm_tops": round(2 * M_PER_RANK * n * k / (tg * 1e-6) / 1e12, 1)})
-        del x, w, wq, ws
+        del x, xb, w, wq, ws
     return rows
 
 

@@ -20,7 +20,7 @@ records their outputs on small seeded inputs:
   two lines (the reference has no function for it) on fp16/bf16 inputs, with
   an all-zero row, a row whose fp16 divisor underflows and near-max values.
   ``--only rowwise`` writes just this file.
-* ``config1.npz`` - the CPU reference workload end to end: x fp32 [256, 5120]
+* ``cpu_workload_256x5120.npz`` - the CPU reference workload end to end: x fp32 [256, 5120]
   N(0,1) with 1 % outlier channels x30, W fp32 [5120, 5120] N(0, 0.02), seed 0;
   Y = dequant(int8 GEMM).  Stored: input checksums, both scale vectors, the
   first rows of the codes and of Y, and Y's Frobenius norm.
@@ -172,7 +172,7 @@ def main(ref_root: str) -> None:
         gemm[f"{name}_y"] = y.numpy() if out == "f32" else _u16(y)
     np.savez_compressed(os.path.join(HERE, "gemm.npz"), **gemm)
 
-    # ---- config 1: the CPU reference workload end to end ------------------------
+    # ---- the CPU reference workload (x [256, 5120], W [5120, 5120]) end to end ------------------------
     x = outlier_activations(256, 5120, seed=0, dtype=torch.float32)
     w = gaussian_weight(5120, 5120, seed=0)
     xq, xs = _eager_quantize(x, 256)
@@ -181,15 +181,15 @@ def main(ref_root: str) -> None:
     dense = x @ w.t()
     rel = ((y - dense).norm() / dense.norm()).item()
     np.savez_compressed(
-        os.path.join(HERE, "config1.npz"),
+        os.path.join(HERE, "cpu_workload_256x5120.npz"),
         x_sha=np.array(_sha(x)), w_sha=np.array(_sha(w)),
         xscale=xs.numpy(), wscale=ws.numpy(),
         xq_head=xq[:8].numpy(), wq_head=wq[:8].numpy(),
         y_head=y[:8].numpy(), y_norm=np.array(y.norm().item()),
         rel_vs_dense=np.array(rel),
     )
-    print("config1 rel-Frobenius vs fp32 dense:", rel)
-    for f in ("quant.npz", "weight.npz", "gemm.npz", "config1.npz"):
+    print("cpu workload rel-Frobenius vs fp32 dense:", rel)
+    for f in ("quant.npz", "weight.npz", "gemm.npz", "cpu_workload_256x5120.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
     rowwise(ref_root)
 

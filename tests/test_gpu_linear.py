@@ -1,9 +1,10 @@
 """End-to-end int8_convrot linear on the GPU through the reference-facing API.
 
 Mirrors the reference's own smoke tests (tests/test_smoke.py:41-91) and adds the
-north-star checks: the dequantised output within 1e-2 relative Frobenius error
-of the reference int8_convrot output (config 1, tests/golden/config1.npz), and
-codes/scales within tolerance of the reference eager path at the DiT sizes.
+parity targets: the dequantised output within 1e-2 relative Frobenius error
+of the reference int8_convrot output (the fp32 CPU workload, x [256, 5120] and
+W [5120, 5120]: tests/golden/cpu_workload_256x5120.npz), and codes/scales
+within tolerance of the reference eager path at the DiT sizes.
 """
 from __future__ import annotations
 
@@ -77,11 +78,11 @@ def test_end_to_end_linear_vs_dense(cuda):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_config1_vs_reference_output(cuda, dtype):
+def test_cpu_workload_vs_reference_output(cuda, dtype):
     """The CPU reference workload (x [256,5120] with outliers, W [5120,5120]) run through
     the kernels in fp16/bf16: output within 1e-2 relative Frobenius of the reference's
-    fp32 int8_convrot output (tests/golden/config1.npz)."""
-    g = np.load(os.path.join(GOLDEN, "config1.npz"))
+    fp32 int8_convrot output (tests/golden/cpu_workload_256x5120.npz)."""
+    g = np.load(os.path.join(GOLDEN, "cpu_workload_256x5120.npz"))
     x = outlier_activations(256, 5120, seed=0, dtype=torch.float32)
     w = gaussian_weight(5120, 5120, seed=0)
     xq, xs = quantize_convrot(x.to(cuda, dtype), G, backend="fht")
@@ -94,11 +95,11 @@ def test_config1_vs_reference_output(cuda, dtype):
     assert np.abs(ws.cpu().numpy() / g["wscale"] - 1).max() < 1e-2
 
 
-def test_config1_fp32_path_matches_reference_bitwise_in_gemm(cuda):
+def test_cpu_workload_fp32_path_matches_reference_bitwise_in_gemm(cuda):
     """fp32 activations take the eager rotation (as in the reference), the GEMM is
     the fused kernel: with the reference's own codes and scales the output is
     bit-identical to the reference's head rows."""
-    g = np.load(os.path.join(GOLDEN, "config1.npz"))
+    g = np.load(os.path.join(GOLDEN, "cpu_workload_256x5120.npz"))
     xq = torch.from_numpy(g["xq_head"]).to(cuda)
     xs = torch.from_numpy(g["xscale"][:8]).to(cuda)
     w = gaussian_weight(5120, 5120, seed=0)

@@ -4,7 +4,7 @@ The oracle (oracle/convrot_oracle.c) restates the reference kernel's arithmetic
 (tilegen/kernels/int8_convrot.py:47-104), so codes and scales must be
 bit-identical.  The golden fixtures pin the reference's eager path
 (_eager_quantize(x.float(), G), int8_convrot.py:289-302); against it the
-north-star tolerance applies: codes equal except +-1 on at most 0.1 % of the
+parity tolerance applies: codes equal except +-1 on at most 0.1 % of the
 elements, scales within 1e-3 relative.
 """
 from __future__ import annotations
@@ -23,8 +23,8 @@ from tilegen_b200.synthetic import dit_activations, outlier_activations
 
 pytestmark = pytest.mark.gpu
 
-CODE_TOL_FRAC = 1e-3   # north star: +-1 on <= 0.1 % of codes
-SCALE_TOL_REL = 1e-3   # north star: scales within 1e-3 relative
+CODE_TOL_FRAC = 1e-3   # parity tolerance: +-1 on <= 0.1 % of codes
+SCALE_TOL_REL = 1e-3   # parity tolerance: scales within 1e-3 relative
 
 
 def _run_and_check(x_cpu: torch.Tensor, group: int, dev):
@@ -92,7 +92,7 @@ def test_bf16_large_magnitudes(cuda):
 
 
 def test_against_reference_golden_vectors(cuda):
-    """The reference eager path's outputs (tests/golden/quant.npz) within the north-star tolerance."""
+    """The reference eager path's outputs (tests/golden/quant.npz) within the parity tolerance (codes +-1 on <= 0.1 %, scales 1e-3 relative)."""
     d = np.load(os.path.join(GOLDEN, "quant.npz"))
     names = sorted({f.split("_")[0] for f in d.files})
     checked = 0

@@ -2,7 +2,7 @@
 
 This pins the oracle before it is trusted as the checker: its rotate+quant must
 reproduce the reference eager path's codes and scales (they agree exactly on
-every fixture case; the north-star tolerance is the bound asserted), and its
+every fixture case; the parity tolerance is the bound asserted), and its
 GEMM + dequant must reproduce int8_matmul_dequant_chunked bit for bit.
 """
 from __future__ import annotations
@@ -55,11 +55,11 @@ def test_gemm_dequant_bit_exact_vs_reference():
         assert np.array_equal(y.view(np.uint8), d[f"{n}_y"].view(np.uint8)), n
 
 
-def test_config1_end_to_end():
+def test_cpu_workload_end_to_end():
     """The CPU reference workload: same seeded inputs, scales and head outputs."""
     from tilegen_b200.synthetic import gaussian_weight, outlier_activations
 
-    g = np.load(os.path.join(GOLDEN, "config1.npz"))
+    g = np.load(os.path.join(GOLDEN, "cpu_workload_256x5120.npz"))
     x = outlier_activations(256, 5120, seed=0, dtype=torch.float32)
     w = gaussian_weight(5120, 5120, seed=0)
     sha = lambda t: hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()

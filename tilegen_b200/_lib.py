@@ -74,7 +74,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
 
 def declared_functions() -> list[str]:
     """Names of the functions ``include/tilegen_b200.h`` declares."""
-    text = open(HEADER).read()
+    with open(HEADER) as f:
+        text = f.read()
     return re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(tg_\w+)\s*\(", text, re.M)
 
 

@@ -12,7 +12,9 @@
 //    TMEM tile (tcgen05 kind::i8, int32).
 //  * K is split: CTA (s, t) multiplies column tile t over k-blocks
 //    [s*kb_per_slice, ...), so that N/128 x slices CTAs stream the weight
-//    from all SMs.
+//    from all SMs.  Each CTA pulls its weight slice into L2 at start-up,
+//    before the programmatic-dependent wait, so that stream overlaps the
+//    activation quantiser launched before it.
 //  * The partial tiles are summed in one of two ways (integer addition: exact
 //    and order-independent either way), then dequantised with one rounding
 //    per operation, as the reference:

@@ -40,6 +40,11 @@ typedef enum { TG_DT_F32 = 0, TG_DT_F16 = 1, TG_DT_BF16 = 2 } tg_dtype;
  * the reference's `input_act`, tilegen/comfyui/backend.py:174,201-204). */
 typedef enum { TG_ACT_NONE = 0, TG_ACT_GELU_TANH = 1, TG_ACT_GELU = 2 } tg_act;
 
+/* OR'ed into tg_quantize_act's `act`: evaluate the rotation in the reference
+ * kernel's butterfly order (bit-identical to it) instead of the default short
+ * order (see tg_rotate_quant). */
+#define TG_QUANT_REFERENCE_ORDER 0x100
+
 /* Library version, (major << 16) | minor. */
 int tg_version(void);
 

@@ -45,6 +45,8 @@ def lib() -> ctypes.CDLL:
         i64, p = ctypes.c_int64, ctypes.c_void_p
         L.oracle_rotate_quant.argtypes = [p, ctypes.c_int, i64, i64, ctypes.c_int, p, p]
         L.oracle_rotate_quant.restype = ctypes.c_int
+        L.oracle_rotate_quant_short.argtypes = [p, ctypes.c_int, i64, i64, ctypes.c_int, p, p]
+        L.oracle_rotate_quant_short.restype = ctypes.c_int
         L.oracle_rowwise_quant.argtypes = [p, ctypes.c_int, i64, i64, p, p]
         L.oracle_rowwise_quant.restype = ctypes.c_int
         L.oracle_int8_gemm_dequant.argtypes = [p, p, p, p, i64, p, i64, i64, i64, ctypes.c_int, p]
@@ -59,17 +61,23 @@ def _ptr(a: np.ndarray) -> int:
     return a.ctypes.data
 
 
-def rotate_quant(x: np.ndarray, dtype: str, group: int = 256):
+def rotate_quant(x: np.ndarray, dtype: str, group: int = 256, order: str = "reference"):
     """Rotate+quantize rows of ``x``.
 
     ``x`` is float32 for ``dtype="float32"``; for ``"float16"``/``"bfloat16"`` it
-    holds the raw 16-bit patterns (uint16/int16).  Returns ``(q int8[M,K], scale f32[M])``.
+    holds the raw 16-bit patterns (uint16/int16).  ``order="reference"`` is the
+    reference kernel's butterfly order (pinned to the golden vectors);
+    ``"short"`` restates the CUDA kernel's default order.  Returns
+    ``(q int8[M,K], scale f32[M])``.
     """
     x = np.ascontiguousarray(x)
     m, k = x.shape
     q = np.empty((m, k), np.int8)
     s = np.empty((m,), np.float32)
-    rc = lib().oracle_rotate_quant(_ptr(x), _DTYPE_CODES[dtype], m, k, group, _ptr(q), _ptr(s))
+    if order not in ("reference", "short"):
+        raise ValueError(f"unknown butterfly order {order!r}")
+    fn = lib().oracle_rotate_quant if order == "reference" else lib().oracle_rotate_quant_short
+    rc = fn(_ptr(x), _DTYPE_CODES[dtype], m, k, group, _ptr(q), _ptr(s))
     if rc != 0:
         raise ValueError(f"oracle_rotate_quant rejected M={m} K={k} group={group}")
     return q, s

@@ -3,7 +3,9 @@
  * checker that the CUDA kernels are compared against, and the CPU baseline that
  * bench.py times.  The product path never calls it.
  *
- * Three functions, each a plain-C restatement of the reference's algorithm:
+ * Three functions, each a plain-C restatement of the reference's algorithm
+ * (plus oracle_rotate_quant_short, the kernels' default butterfly order,
+ * described where it is defined):
  *
  *  oracle_rotate_quant  - tilegen/kernels/int8_convrot.py:47-104 (`fht_quant`):
  *      per 256-wide group, four radix-4 butterfly stages on the (non-Sylvester)
@@ -180,6 +182,77 @@ int oracle_rotate_quant(const void *x, int dtype, int64_t M, int64_t K, int grou
             for (int i = 0; i < group; ++i) {
                 float v = nearbyintf(grp[i] * inv);
                 v = fminf(fmaxf(v, -128.0f), 127.0f);
+                q[m * K + g0 + i] = (int8_t)v;
+            }
+        }
+    }
+    return 0;
+}
+
+/* The kernel's default ("short") butterfly order, restated: per radix-4
+ * butterfly S = (a0 + a2) + (a1 + a3) and output 3 - i = fma(-2, a_i, S) --
+ * the same H4 (every row all ones but a single -1) with fewer roundings.  Not
+ * the reference's order: parity with the reference is the north-star
+ * tolerance (codes +-1 on <= 0.1 %, scales 1e-3 relative), checked in the
+ * tests against oracle_rotate_quant and the golden vectors. */
+static void rotate_group_short(float *grp, int group, int nst) {
+    for (int st = 0; st < nst; ++st) {
+        const int stride = 1 << (2 * st);
+        for (int b = 0; b < group / 4; ++b) {
+            const int low = b % stride;
+            const int high = b / stride;
+            const int base = high * 4 * stride + low;
+            const float a0 = grp[base];
+            const float a1 = grp[base + stride];
+            const float a2 = grp[base + 2 * stride];
+            const float a3 = grp[base + 3 * stride];
+            const float s = (a0 + a2) + (a1 + a3);
+            grp[base] = fmaf(-2.0f, a3, s);
+            grp[base + stride] = fmaf(-2.0f, a2, s);
+            grp[base + 2 * stride] = fmaf(-2.0f, a1, s);
+            grp[base + 3 * stride] = fmaf(-2.0f, a0, s);
+        }
+    }
+}
+
+/* Rotate+quant in the short order.  Scale as oracle_rotate_quant (absmax with
+ * NaN ignored).  Codes of a row whose rotated values are all finite:
+ * rint(v * inv) of the exact product (one fma with 1.5 * 2^23, as the kernel
+ * does); any other row: clamp(rint(v * inv)) with the product rounded first
+ * and NaN -> -128, as oracle_rotate_quant. */
+int oracle_rotate_quant_short(const void *x, int dtype, int64_t M, int64_t K, int group,
+                              int8_t *q, float *scale) {
+    const int nst = group_stages(group);
+    if (nst < 0 || K <= 0 || K % group) return -1;
+    const float root = (float)(1 << nst);
+    const float qmax_root = 127.0f * root;
+#pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m) {
+        float grp[256];
+        float amax = 0.0f;
+        int finite = 1;
+        for (int64_t g0 = 0; g0 < K; g0 += group) {
+            for (int i = 0; i < group; ++i) grp[i] = load_elem(x, dtype, m * K + g0 + i);
+            rotate_group_short(grp, group, nst);
+            for (int i = 0; i < group; ++i) {
+                amax = fmaxf(amax, fabsf(grp[i]));
+                if (!isfinite(grp[i])) finite = 0;
+            }
+        }
+        const float s = fmaxf(amax / qmax_root, 1e-30f);
+        scale[m] = s;
+        const float inv = 1.0f / (s * root);
+        for (int64_t g0 = 0; g0 < K; g0 += group) {
+            for (int i = 0; i < group; ++i) grp[i] = load_elem(x, dtype, m * K + g0 + i);
+            rotate_group_short(grp, group, nst);
+            for (int i = 0; i < group; ++i) {
+                float v;
+                if (finite) {
+                    v = fmaf(grp[i], inv, 12582912.0f) - 12582912.0f;
+                } else {
+                    v = nearbyintf(grp[i] * inv);
+                    v = fminf(fmaxf(v, -128.0f), 127.0f);
+                }
                 q[m * K + g0 + i] = (int8_t)v;
             }
         }

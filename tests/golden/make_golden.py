@@ -1,8 +1,9 @@
 """Generate the golden fixtures in this folder from the reference implementation.
 
-Run from the repository root in a container that has the reference sources:
+Run from the repository root in a container that has the reference sources,
+passing the reference checkout's root (required):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference root> [--only rowwise|weight16]
 
 It imports the reference's own pure-torch functions (they run on the CPU) and
 records their outputs on small seeded inputs:
@@ -12,6 +13,10 @@ records their outputs on small seeded inputs:
   with zeros, tiny and huge values.
 * ``weight.npz``  - ``tilegen.quant.weight.quantize_convrot_weight(W, 256)``
   (weight.py:14-39) on fp32 weights.
+* ``weight16.npz`` - the same on fp32 weights whose values are exactly fp16
+  (``f16_*``) or bf16 (``bf16_*``) numbers, so that the GPU kernel, which reads
+  the 16-bit tensor, sees the reference's inputs exactly.  ``--only weight16``
+  writes just this file.
 * ``gemm.npz``    - ``tilegen.quant.int8_ops.int8_matmul_dequant_chunked``
   (int8_ops.py:22-70) through CPU ``torch._int_mm``: fp16/bf16/fp32 outputs,
   with and without bias, per-channel and scalar weight scales, small chunk caps.
@@ -103,6 +108,24 @@ def rowwise(ref_root: str) -> None:
     print("rowwise.npz", os.path.getsize(os.path.join(HERE, "rowwise.npz")), "bytes")
 
 
+def weight16(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    sys.path.append(REPO)
+    from tilegen.quant.weight import quantize_convrot_weight  # reference
+    assert os.path.realpath(sys.modules["tilegen"].__file__).startswith(os.path.realpath(ref_root))
+    from tilegen_b200.synthetic import gaussian_weight
+
+    out = {}
+    for name, dt in (("f16", torch.float16), ("bf16", torch.bfloat16)):
+        w16 = gaussian_weight(16, 5120, seed=12, dtype=dt)
+        wq, ws = quantize_convrot_weight(w16.float(), 256)
+        out[f"{name}_w"] = _u16(w16)
+        out[f"{name}_wq"] = wq.numpy()
+        out[f"{name}_wscale"] = ws.numpy()
+    np.savez_compressed(os.path.join(HERE, "weight16.npz"), **out)
+    print("weight16.npz", os.path.getsize(os.path.join(HERE, "weight16.npz")), "bytes")
+
+
 def main(ref_root: str) -> None:
     sys.path.insert(0, ref_root)
     sys.path.append(REPO)
@@ -192,12 +215,18 @@ def main(ref_root: str) -> None:
     for f in ("quant.npz", "weight.npz", "gemm.npz", "cpu_workload_256x5120.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
     rowwise(ref_root)
+    weight16(ref_root)
 
 
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    root = args[0] if args else "/root/reference"
-    if "--only" in sys.argv and sys.argv[-1] == "rowwise":
+    if not args or args[0] in ("rowwise", "weight16"):
+        sys.exit("usage: make_golden.py <reference root> [--only rowwise|weight16]")
+    root = args[0]
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+    if only == "rowwise":
         rowwise(root)
+    elif only == "weight16":
+        weight16(root)
     else:
         main(root)

@@ -58,7 +58,7 @@ def test_fused_act_equals_act_then_quantise(cuda, act, dtype, group):
         rq, rs = ops.rotate_quant(xa, group)
         torch.cuda.synchronize()
         _assert_same(q, s, rq, rs, f"{act} {dtype} G={group} M={m} K={k}")
-        oq, os_ = oracle.rotate_quant(raw16(xa), DT_NAME[dtype], group)
+        oq, os_ = oracle.rotate_quant(raw16(xa), DT_NAME[dtype], group, order="short")
         assert np.array_equal(q.cpu().numpy(), oq) and np.array_equal(s.cpu().numpy(), os_)
 
 

@@ -14,8 +14,9 @@ import numpy as np
 import pytest
 import torch
 
+import oracle
 import tilegen  # the drop-in alias package
-from tests._util import rel_fro
+from tests._util import raw16, rel_fro
 from tests.conftest import GOLDEN
 from tilegen.kernels.hadamard import build_hadamard, rotate_by_group
 from tilegen.kernels.int8_convrot import _eager_quantize, can_use_fht, quantize_convrot, quantize_convrot_fht
@@ -47,6 +48,84 @@ def test_weight_quant_shape_and_dtype(cuda):
     assert wscale.shape == (5120,) and wscale.dtype == torch.float32
 
 
+def test_weight_quant_kernel_path_bit_exact_full_qkv_weight(cuda):
+    """quantize_convrot_weight on a CUDA bf16 [15360, 5120] weight (the qkv projection) runs
+    the rotate+quant kernel: bit-identical to the oracle's restatement of the kernel's order,
+    and within the parity tolerance of the reference order (weight.py:14-39)."""
+    w = gaussian_weight(15360, 5120, seed=3, dtype=torch.bfloat16, device=cuda)
+    wq, ws = quantize_convrot_weight(w, G)
+    wq, ws = wq.cpu().numpy(), ws.cpu().numpy()
+    rq, rs = oracle.rotate_quant(raw16(w), "bfloat16", G, order="short")
+    assert np.array_equal(wq, rq) and np.array_equal(ws.view(np.uint32), rs.view(np.uint32))
+    eq, es = oracle.rotate_quant(raw16(w), "bfloat16", G, order="reference")
+    d = np.abs(wq.astype(np.int32) - eq.astype(np.int32))
+    assert d.max() <= 1 and (d > 0).mean() <= 1e-3 and (np.abs(ws - es) / es).max() <= 1e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_weight_quant_kernel_path_vs_reference_outputs(cuda, dtype):
+    """The reference's quantize_convrot_weight outputs on fp16/bf16-valued weights
+    (tests/golden/weight16.npz) against the kernel path: codes +-1 on <= 0.1 %, scales 1e-3 rel."""
+    d = np.load(os.path.join(GOLDEN, "weight16.npz"))
+    name = "f16" if dtype == torch.float16 else "bf16"
+    w = torch.from_numpy(d[f"{name}_w"].view(np.int16)).view(dtype).to(cuda)
+    wq, ws = quantize_convrot_weight(w, G)
+    dq = np.abs(wq.cpu().numpy().astype(np.int32) - d[f"{name}_wq"].astype(np.int32))
+    assert dq.max() <= 1 and (dq > 0).mean() <= 1e-3
+    assert (np.abs(ws.cpu().numpy() - d[f"{name}_wscale"]) / d[f"{name}_wscale"]).max() <= 1e-3
+
+
+def test_weight_quant_fp32_path_vs_reference_outputs(cuda):
+    """fp32 weights take the reference's own torch sequence (tests/golden/weight.npz)."""
+    d = np.load(os.path.join(GOLDEN, "weight.npz"))
+    wq, ws = quantize_convrot_weight(torch.from_numpy(d["w"]).to(cuda), G)
+    dq = np.abs(wq.cpu().numpy().astype(np.int32) - d["wq"].astype(np.int32))
+    assert dq.max() <= 1 and (dq > 0).mean() <= 1e-3
+    assert (np.abs(ws.cpu().numpy() - d["wscale"]) / d["wscale"]).max() <= 1e-3
+
+
+def _torch_gemm_sequence(xq, xs, wq, ws, out_dtype):
+    """The reference's GEMM + dequant (int8_ops.py:60-68) as torch runs it on the GPU, unchunked."""
+    part = torch._int_mm(xq, wq.t()).float()
+    part.mul_(xs.float().reshape(-1, 1))
+    part.mul_(ws.float().reshape(1, -1))
+    return part.to(out_dtype)
+
+
+@pytest.mark.parametrize("name,k,n", DIT_SHAPES)
+def test_dit_block_linear_8190_rows_bf16(cuda, name, k, n):
+    """The DiT-block workload at 8 GPUs: 65520 tokens / 8 = 8190 bf16 rows per GPU (not a
+    multiple of 128), each projection through the reference-facing calls.
+    * activation and weight codes/scales: bit-identical to the oracle (kernel order) and
+      within tolerance of the reference order;
+    * output: bit-identical to the reference's torch GEMM sequence on the same codes, and
+      to the oracle's GEMM + dequant on the first and last (ragged-tile) rows;
+    * output within 1e-2 relative Frobenius of the reference int8_convrot output (the
+      reference order's codes through the same exact GEMM)."""
+    m = 8190
+    x = dit_activations(name, m, seed=5, dtype=torch.bfloat16, device=cuda)
+    w = gaussian_weight(n, k, seed=6, dtype=torch.bfloat16, device=cuda)
+    xq, xs = quantize_convrot(x, G, backend="fht")
+    wq, ws = quantize_convrot_weight(w, G)
+    y = int8_matmul_dequant_chunked(xq, xs, wq, ws, None, torch.bfloat16)
+    torch.cuda.synchronize()
+    xr = raw16(x)
+    oq, os_ = oracle.rotate_quant(xr, "bfloat16", G, order="short")
+    assert np.array_equal(xq.cpu().numpy(), oq) and np.array_equal(xs.cpu().numpy().view(np.uint32), os_.view(np.uint32))
+    ow, ows = oracle.rotate_quant(raw16(w), "bfloat16", G, order="short")
+    assert np.array_equal(wq.cpu().numpy(), ow) and np.array_equal(ws.cpu().numpy(), ows)
+    ref = _torch_gemm_sequence(xq, xs, wq, ws, torch.bfloat16)
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+    rows = np.r_[0:4, m - 6:m]
+    oy = oracle.int8_gemm_dequant(oq[rows], os_[rows], ow, ows, None, "bfloat16")
+    assert np.array_equal(raw16(y[torch.from_numpy(rows).to(cuda)]), oy)
+    eq, es = oracle.rotate_quant(xr, "bfloat16", G, order="reference")
+    dq = np.abs(oq.astype(np.int32) - eq.astype(np.int32))
+    assert dq.max() <= 1 and (dq > 0).mean() <= 1e-3 and (np.abs(os_ - es) / es).max() <= 1e-3
+    y_ref = _torch_gemm_sequence(torch.from_numpy(eq).to(cuda), torch.from_numpy(es).to(cuda), wq, ws, torch.float32)
+    assert rel_fro(y.float().cpu(), y_ref.cpu()) <= 1e-2
+
+
 def test_fht_vs_eager_numerics(cuda):
     """The reference's own check (test_smoke.py:62-68) against its fp16 eager path."""
     x = torch.randn(2048, 5120, device=cuda, dtype=DT) * 0.1
@@ -62,6 +141,11 @@ def test_can_use_fht_thresholds(cuda):
     assert can_use_fht(x_cuda.cpu(), 256) is False
     assert can_use_fht(x_cuda, 128, min_k=0) is False
     assert can_use_fht(x_cuda, 256, min_k=99999) is False
+    # the reference's rule: other groups go to the eager path (in x's dtype)
+    assert can_use_fht(x_cuda, 64, min_k=0) is False
+    xq, xs = quantize_convrot(x_cuda, 64)
+    eq, es = _eager_quantize(x_cuda, 64)
+    assert torch.equal(xq, eq) and torch.equal(xs, es)
 
 
 def test_end_to_end_linear_vs_dense(cuda):

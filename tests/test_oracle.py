@@ -39,6 +39,66 @@ def test_rotate_quant_matches_reference_eager():
         assert np.array_equal(q, rq), n
 
 
+@pytest.mark.parametrize("order", ["reference", "short"])
+def test_both_orders_within_tolerance_of_reference_eager(order):
+    """Both butterfly orders against the reference eager path: codes +-1 on <= 0.1 %,
+    scales 1e-3 relative (the parity tolerance; observed: identical codes)."""
+    d, names = _quant_cases()
+    for n in names:
+        m, k, g, dt = (int(v) for v in d[f"{n}_meta"])
+        q, s = oracle.rotate_quant(d[f"{n}_x"], DT_NAMES[dt], g, order=order)
+        diff = np.abs(q.astype(np.int32) - d[f"{n}_q"].astype(np.int32))
+        assert diff.max() <= 1 and (diff > 0).mean() <= 1e-3, n
+        assert (np.abs(s - d[f"{n}_scale"]) / d[f"{n}_scale"]).max() <= 1e-3, n
+
+
+def test_short_order_vs_reference_order_on_dit_activations():
+    """The kernel's default order against the reference kernel's order on 256 x 13824
+    GELU activations and 256 x 5120 outlier activations: within tolerance."""
+    from tests._util import raw16
+    from tilegen_b200.synthetic import dit_activations
+
+    for name, dt in (("ffn_down", torch.bfloat16), ("qkv_proj", torch.float16)):
+        x = raw16(dit_activations(name, 256, seed=3, dtype=dt))
+        dn = "bfloat16" if dt == torch.bfloat16 else "float16"
+        q, s = oracle.rotate_quant(x, dn, 256, order="short")
+        rq, rs = oracle.rotate_quant(x, dn, 256, order="reference")
+        diff = np.abs(q.astype(np.int32) - rq.astype(np.int32))
+        assert diff.max() <= 1 and (diff > 0).mean() <= 1e-3
+        assert (np.abs(s - rs) / rs).max() <= 1e-3
+
+
+def test_short_order_planted_mistake_is_caught():
+    """The short order's outputs come out digit-reversed (output 3 - i at input i);
+    a copy that forgets the reversal (planted here, in numpy) gives other codes."""
+    x = np.random.default_rng(1).standard_normal((4, 256)).astype(np.float32)
+    q, s = oracle.rotate_quant(x, "float32", 256, order="short")
+    y = x.copy()
+    for st in range(4):
+        st_s = 1 << (2 * st)
+        for b in range(64):
+            base = (b // st_s) * 4 * st_s + b % st_s
+            a = [y[:, base + i * st_s].copy() for i in range(4)]
+            tot = (a[0] + a[2]) + (a[1] + a[3])
+            for i in range(4):
+                y[:, base + i * st_s] = tot - np.float32(2) * a[i]  # planted: should be a[3 - i]
+    inv = (np.float32(1) / (s * np.float32(16))).astype(np.float32)
+    bad = np.clip(np.rint((y * inv[:, None]).astype(np.float32)), -128, 127).astype(np.int8)
+    assert (bad != q).mean() > 0.5
+
+
+def test_weight16_fixture_both_orders():
+    """fp16/bf16-valued weights quantised by the reference in fp32 (tests/golden/weight16.npz):
+    both orders within the parity tolerance."""
+    d = np.load(os.path.join(GOLDEN, "weight16.npz"))
+    for name, dt in (("f16", "float16"), ("bf16", "bfloat16")):
+        for order in ("reference", "short"):
+            q, s = oracle.rotate_quant(d[f"{name}_w"], dt, 256, order=order)
+            diff = np.abs(q.astype(np.int32) - d[f"{name}_wq"].astype(np.int32))
+            assert diff.max() <= 1 and (diff > 0).mean() <= 1e-3, (name, order)
+            assert (np.abs(s - d[f"{name}_wscale"]) / d[f"{name}_wscale"]).max() <= 1e-3, (name, order)
+
+
 def test_weight_quant_matches_reference():
     d = np.load(os.path.join(GOLDEN, "weight.npz"))
     q, s = oracle.rotate_quant(d["w"], "float32", 256)

@@ -34,6 +34,7 @@ TG_ERR_DEVICE_TIMEOUT = 5
 
 TG_DT_F32, TG_DT_F16, TG_DT_BF16 = 0, 1, 2
 TG_ACT_NONE, TG_ACT_GELU_TANH, TG_ACT_GELU = 0, 1, 2
+TG_QUANT_REFERENCE_ORDER = 0x100  # OR'ed into tg_quantize_act's act: the reference butterfly order
 
 _lock = threading.Lock()
 _lib = None

@@ -75,11 +75,11 @@ bool ensure_smem_attr(K kernel, int dev, uint32_t bytes, uint32_t* done_bytes) {
 }
 
 // ------------------------------------------------------------------ rotate+quant
-template <int NST, bool BF16, int ACT>
+template <int NST, bool BF16, int ACT, bool EXACT>
 int launch_rotquant_t(const CUtensorMap& tm, const tg::RotQuantParams& p, int threads, uint32_t smem, int dev,
                       int sms, cudaStream_t st) {
   static uint32_t attr_done[kMaxDevices];
-  auto kern = tg::rotquant_kernel<NST, BF16, ACT>;
+  auto kern = tg::rotquant_kernel<NST, BF16, ACT, EXACT>;
   if (!ensure_smem_attr(kern, dev, smem, attr_done)) return TG_ERR_CUDA;
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem) != cudaSuccess || occ < 1)
@@ -99,13 +99,27 @@ int launch_rotquant_t(const CUtensorMap& tm, const tg::RotQuantParams& p, int th
   return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
 }
 
-template <int NST, bool BF16>
+template <int NST, bool BF16, bool EXACT>
 int launch_rotquant_act(int act, const CUtensorMap& tm, const tg::RotQuantParams& p, int threads, uint32_t smem,
                         int dev, int sms, cudaStream_t st) {
   switch (act) {
-    case TG_ACT_GELU_TANH: return launch_rotquant_t<NST, BF16, tg::kActGeluTanh>(tm, p, threads, smem, dev, sms, st);
-    case TG_ACT_GELU: return launch_rotquant_t<NST, BF16, tg::kActGelu>(tm, p, threads, smem, dev, sms, st);
-    default: return launch_rotquant_t<NST, BF16, tg::kActNone>(tm, p, threads, smem, dev, sms, st);
+    case TG_ACT_GELU_TANH:
+      return launch_rotquant_t<NST, BF16, tg::kActGeluTanh, EXACT>(tm, p, threads, smem, dev, sms, st);
+    case TG_ACT_GELU: return launch_rotquant_t<NST, BF16, tg::kActGelu, EXACT>(tm, p, threads, smem, dev, sms, st);
+    default: return launch_rotquant_t<NST, BF16, tg::kActNone, EXACT>(tm, p, threads, smem, dev, sms, st);
+  }
+}
+
+// The butterfly order: the reference kernel's (bit-identical to it) or the
+// short one (the default).  The rotation-free form has no butterflies.
+template <int NST, bool BF16>
+int launch_rotquant_order(bool exact, int act, const CUtensorMap& tm, const tg::RotQuantParams& p, int threads,
+                          uint32_t smem, int dev, int sms, cudaStream_t st) {
+  if constexpr (NST == 0) {
+    return launch_rotquant_act<NST, BF16, true>(act, tm, p, threads, smem, dev, sms, st);
+  } else {
+    if (exact) return launch_rotquant_act<NST, BF16, true>(act, tm, p, threads, smem, dev, sms, st);
+    return launch_rotquant_act<NST, BF16, false>(act, tm, p, threads, smem, dev, sms, st);
   }
 }
 
@@ -151,6 +165,8 @@ int tg_quantize_act(const void* x, int x_dtype, int64_t M, int64_t K, int group,
                     void* stream) {
   if (M < 0 || K <= 0) return TG_ERR_INVALID_ARG;
   if (x_dtype != TG_DT_F16 && x_dtype != TG_DT_BF16) return TG_ERR_INVALID_ARG;
+  const bool exact = (act & TG_QUANT_REFERENCE_ORDER) != 0;
+  act &= ~TG_QUANT_REFERENCE_ORDER;
   if (act != TG_ACT_NONE && act != TG_ACT_GELU_TANH && act != TG_ACT_GELU) return TG_ERR_INVALID_ARG;
   int nst;
   switch (group) {
@@ -199,10 +215,10 @@ int tg_quantize_act(const void* x, int x_dtype, int64_t M, int64_t K, int group,
   // budget allows per SM (96 registers a thread) still fit in shared memory.
   int ctas = 65536 / (threads * kRotQuantRegs);
   ctas = ctas < 1 ? 1 : ctas;
-  const uint32_t per_cta = 232448u / uint32_t(ctas) - 2048u - 1024u - uint32_t(3 * R) * 4u;
+  const uint32_t per_cta = 232448u / uint32_t(ctas) - 2048u - 1024u - uint32_t(6 * R) * 4u;
   int stages = int(per_cta / stage_bytes);
   stages = stages < 2 ? 2 : (stages > 4 ? 4 : stages);
-  const uint32_t smem = 1024u + uint32_t(stages) * stage_bytes + uint32_t(stages) * 8u + uint32_t(3 * R) * 4u;
+  const uint32_t smem = 1024u + uint32_t(stages) * stage_bytes + uint32_t(stages) * 8u + uint32_t(6 * R) * 4u;
 
   int dev;
   DeviceInfo info;
@@ -230,18 +246,18 @@ int tg_quantize_act(const void* x, int x_dtype, int64_t M, int64_t K, int group,
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf = x_dtype == TG_DT_BF16;
-#define TG_RQ_CASE(N)                                                                        \
-  case N:                                                                                    \
-    return bf ? launch_rotquant_act<N, true>(act, tm, p, threads, smem, dev, info.sms, st) \
-              : launch_rotquant_act<N, false>(act, tm, p, threads, smem, dev, info.sms, st);
+#define TG_RQ_CASE(N)                                                                                 \
+  case N:                                                                                             \
+    return bf ? launch_rotquant_order<N, true>(exact, act, tm, p, threads, smem, dev, info.sms, st) \
+              : launch_rotquant_order<N, false>(exact, act, tm, p, threads, smem, dev, info.sms, st);
   switch (nst) {
     TG_RQ_CASE(0)
     TG_RQ_CASE(1)
     TG_RQ_CASE(2)
     TG_RQ_CASE(3)
     default:
-      return bf ? launch_rotquant_act<4, true>(act, tm, p, threads, smem, dev, info.sms, st)
-                : launch_rotquant_act<4, false>(act, tm, p, threads, smem, dev, info.sms, st);
+      return bf ? launch_rotquant_order<4, true>(exact, act, tm, p, threads, smem, dev, info.sms, st)
+                : launch_rotquant_order<4, false>(exact, act, tm, p, threads, smem, dev, info.sms, st);
   }
 #undef TG_RQ_CASE
 }

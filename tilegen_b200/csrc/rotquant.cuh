@@ -129,6 +129,60 @@ __device__ __forceinline__ float absmax3(float m, float a, float b) {
   return r;
 }
 
+// The same with NaN propagating: NaN when any operand is NaN.
+__device__ __forceinline__ float absmax3_nan(float m, float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(m), "f"(fabsf(a)), "f"(fabsf(b)));
+  return r;
+}
+
+// ---- the short butterfly (default order) -------------------------------------
+// The same H4 product with fewer roundings per output:
+//   S = (a0 + a2) + (a1 + a3),   y_{3-i} = S - 2 a_i   (one fma each),
+// because every row of the H4 is all ones but one -1, at column 3 - i for row i.
+// Written in place, position i of the digit ends up holding output 3 - i, so
+// after all stages of a group position P holds output G - 1 - P (each base-4
+// digit reversed); the stores undo that.  3 adds and 4 fmas per 4 outputs
+// against the 10 adds of the reference order; the results differ from that
+// order by a few fp32 ulps, so codes can differ by one at rounding ties.
+__device__ __forceinline__ void bfly4x2_short(float2& a0, float2& a1, float2& a2, float2& a3) {
+  const float2 s = add2(add2(a0, a2), add2(a1, a3));
+  const float2 m2 = make_float2(-2.0f, -2.0f);
+  a0 = fma2(a0, m2, s);
+  a1 = fma2(a1, m2, s);
+  a2 = fma2(a2, m2, s);
+  a3 = fma2(a3, m2, s);
+}
+
+// One butterfly whose inputs are two pairs p0 = (a0, a1), p1 = (a2, a3):
+// t = (a0 + a2, a1 + a3) paired, S formed in both lanes (t.x + t.y and
+// t.y + t.x are the same IEEE sum), then the two fmas paired.
+__device__ __forceinline__ void bfly4_short(float2& p0, float2& p1) {
+  const float2 t = add2(p0, p1);
+  const float2 s = make_float2(__fadd_rn(t.x, t.y), __fadd_rn(t.y, t.x));
+  const float2 m2 = make_float2(-2.0f, -2.0f);
+  p0 = fma2(p0, m2, s);
+  p1 = fma2(p1, m2, s);
+}
+
+__device__ __forceinline__ void stage0_64_short(float2 (&vp)[32]) {
+#pragma unroll
+  for (int h = 0; h < 16; ++h) bfly4_short(vp[2 * h], vp[2 * h + 1]);
+}
+
+__device__ __forceinline__ void stage1_64_short(float2 (&vp)[32]) {
+#pragma unroll
+  for (int h = 0; h < 4; ++h)
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+      bfly4x2_short(vp[8 * h + u], vp[8 * h + 2 + u], vp[8 * h + 4 + u], vp[8 * h + 6 + u]);
+}
+
+__device__ __forceinline__ void stage2_64_short(float2 (&vp)[32]) {
+#pragma unroll
+  for (int l = 0; l < 8; ++l) bfly4x2_short(vp[l], vp[l + 8], vp[l + 16], vp[l + 24]);
+}
+
 // The thread's 64 values are held as 32 pairs vp[k] = (v[2k], v[2k+1]).
 // Stage 0 (stride 1) pairs two inputs of one butterfly, so it runs scalar;
 // stages 1 and 2 (strides 4 and 16) pair the butterflies at positions p and
@@ -240,6 +294,61 @@ __device__ __forceinline__ uint32_t pack4(uint2 a, uint2 b) {
   return __byte_perm(__byte_perm(a.x, a.y, 0x0040), __byte_perm(b.x, b.y, 0x0040), 0x5410);
 }
 
+// Codes of a row whose rotated values are all finite (no clamp needed, see
+// code_bits2): rint(x*inv) as one f32x2 fma with 1.5*2^23, the product not
+// rounded on its own, so a product within an fp32 ulp of a half-integer can
+// round the other way than code_bits2's.
+__device__ __forceinline__ uint2 code_bits2_fused(float2 x, float2 inv2) {
+  const float2 t = fma2(x, inv2, make_float2(12582912.0f, 12582912.0f));
+  return make_uint2(__float_as_uint(t.x), __float_as_uint(t.y));
+}
+
+// Four codes of positions 4w..4w+3 (pairs a = (4w, 4w+1), b = (4w+2, 4w+3))
+// packed in reverse: byte 0 is position 4w+3.
+__device__ __forceinline__ uint32_t pack4_rev(uint2 a, uint2 b) {
+  return pack4(make_uint2(b.y, b.x), make_uint2(a.y, a.x));
+}
+
+template <bool FUSED>
+__device__ __forceinline__ uint2 codes2(float2 x, float2 inv2) {
+  return FUSED ? code_bits2_fused(x, inv2) : code_bits2(x, inv2);
+}
+
+// Codes of one line in output order from the short order's reversed
+// positions.  NST == 4: vp is spent and w2[c][jp] holds positions
+// c*64 + 16*qd + 2*jp + {0, 1} of the group (qd: the thread's column block),
+// i.e. outputs (3-c)*64 + 16*(3-qd) + 15 - 2*jp - {0, 1}; qp points at the
+// output block 16*(3-qd) of the group and output quarter r comes from c = 3-r.
+// NST < 4: position p of the line holds output p ^ (G - 1), so output word w
+// (outputs 4w..4w+3) is position word w ^ ((G - 1) >> 2), bytes reversed.
+template <int NST, bool FUSED>
+__device__ __forceinline__ void store_codes_short(int8_t* qp, const float2 (&vp)[32], const float2 (&w2)[4][8],
+                                                  float2 inv2) {
+  if (NST == 4) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int c = 3 - r;
+      uint32_t wd[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        wd[k] = pack4_rev(codes2<FUSED>(w2[c][6 - 2 * k], inv2), codes2<FUSED>(w2[c][7 - 2 * k], inv2));
+      *reinterpret_cast<uint4*>(qp + r * 64) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    }
+  } else {
+    constexpr int XW = ((1 << (2 * NST)) - 1) >> 2;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t wd[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int pw = (4 * c + k) ^ XW;
+        wd[k] = pack4_rev(codes2<FUSED>(vp[2 * pw], inv2), codes2<FUSED>(vp[2 * pw + 1], inv2));
+      }
+      *reinterpret_cast<uint4*>(qp + c * 16) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    }
+  }
+}
+
 // Codes of the rotation-free branch: int8(clamp(round(dtype(v / d)), -128, 127))
 // with d the scale rounded to x's dtype, the division IEEE fp32 (torch's
 // op-math), dtype() rounding to x's dtype, round() half to even, clamp keeping
@@ -289,7 +398,7 @@ __device__ __forceinline__ uint32_t rowwise_codes4(float2 a, float2 b, float2 rc
   return __byte_perm(*reinterpret_cast<const uint32_t*>(&ha), *reinterpret_cast<const uint32_t*>(&hb), 0x6420);
 }
 
-template <int NST, bool BF16, int ACT>
+template <int NST, bool BF16, int ACT, bool EXACT>
 __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
                                                        const RotQuantParams p) {
   constexpr float kRoot = float(1 << NST);               // sqrt(G)
@@ -315,7 +424,7 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
   float* const sout = p.scale;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(stages) * stage_bytes);
-  unsigned* rowmax = reinterpret_cast<unsigned*>(full + stages);  // [3][R]
+  unsigned* rowmax = reinterpret_cast<unsigned*>(full + stages);  // [3][R] maxima, then [3][R] NaN flags
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x;
@@ -328,7 +437,7 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
     fence_mbar_init();
     abort_flag = 0;
   }
-  for (int i = tid; i < 3 * R; i += blockDim.x) rowmax[i] = 0u;
+  for (int i = tid; i < 6 * R; i += blockDim.x) rowmax[i] = 0u;
   __syncthreads();
   // Let the next kernel in the stream (the GEMM) be scheduled as SMs free up;
   // it waits for this grid's completion before reading the codes.  Then wait
@@ -371,6 +480,8 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
   // Codes of this thread: NST == 4 writes one 16-value block per output
   // quarter of its group (stride 64), else its own 64 contiguous values.
   const int code_off = NST == 4 ? (chunk >> 2) * 256 + (chunk & 3) * 16 : chunk * 64;
+  // The short order's reversed positions put NST == 4's block at 3 - qd.
+  const int code_off_short = NST == 4 ? (chunk >> 2) * 256 + (3 - (chunk & 3)) * 16 : chunk * 64;
 
   int s = 0;
   uint32_t parity = 0;
@@ -391,11 +502,21 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
         unpack8<BF16, ACT>(w, &vp[4 * c]);
       }
     }
-    if (NST >= 1) stage0_64(vp);
-    if (NST >= 2) stage1_64(vp);
-    if (NST >= 3) stage2_64(vp);
+    if (EXACT) {
+      if (NST >= 1) stage0_64(vp);
+      if (NST >= 2) stage1_64(vp);
+      if (NST >= 3) stage2_64(vp);
+    } else {
+      if (NST >= 1) stage0_64_short(vp);
+      if (NST >= 2) stage1_64_short(vp);
+      if (NST >= 3) stage2_64_short(vp);
+    }
 
     float amax;
+    // Short order: the thread's own values held a NaN.  Its absmax is then
+    // taken again with NaN ignored (as the reference's fmaxf does) and the row
+    // is flagged so that its codes take the clamped form.
+    bool has_nan = false;
     float2 w2[4][8];  // NST == 4 only: [input c][column pair] of this thread's block
     if (NST == 4) {
       // Swap 16-value blocks among the four threads of a group through this
@@ -423,11 +544,29 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
       float am4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int jp = 0; jp < 8; ++jp) {
-        bfly4x2(w2[0][jp], w2[1][jp], w2[2][jp], w2[3][jp]);
+        if (EXACT) {
+          bfly4x2(w2[0][jp], w2[1][jp], w2[2][jp], w2[3][jp]);
 #pragma unroll
-        for (int r = 0; r < 4; ++r) am4[r] = absmax3(am4[r], w2[r][jp].x, w2[r][jp].y);
+          for (int r = 0; r < 4; ++r) am4[r] = absmax3(am4[r], w2[r][jp].x, w2[r][jp].y);
+        } else {
+          bfly4x2_short(w2[0][jp], w2[1][jp], w2[2][jp], w2[3][jp]);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) am4[r] = absmax3_nan(am4[r], w2[r][jp].x, w2[r][jp].y);
+        }
       }
-      amax = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
+      if (EXACT) {
+        amax = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
+      } else {
+        amax = max_nan(max_nan(am4[0], am4[1]), max_nan(am4[2], am4[3]));
+        if (amax != amax) {
+          has_nan = true;
+          amax = 0.0f;
+#pragma unroll
+          for (int jp = 0; jp < 8; ++jp)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) amax = absmax3(amax, w2[r][jp].x, w2[r][jp].y);
+        }
+      }
     } else if (NST == 0) {
       float am4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
@@ -436,9 +575,21 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
       amax = max_nan(max_nan(am4[0], am4[1]), max_nan(am4[2], am4[3]));
     } else {
       float am4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (EXACT) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) am4[i & 3] = absmax3(am4[i & 3], vp[i].x, vp[i].y);
-      amax = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
+        for (int i = 0; i < 32; ++i) am4[i & 3] = absmax3(am4[i & 3], vp[i].x, vp[i].y);
+        amax = fmaxf(fmaxf(am4[0], am4[1]), fmaxf(am4[2], am4[3]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) am4[i & 3] = absmax3_nan(am4[i & 3], vp[i].x, vp[i].y);
+        amax = max_nan(max_nan(am4[0], am4[1]), max_nan(am4[2], am4[3]));
+        if (amax != amax) {
+          has_nan = true;
+          amax = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) amax = absmax3(amax, vp[i].x, vp[i].y);
+        }
+      }
     }
 
     // ---- row absmax -----------------------------------------------------------
@@ -449,7 +600,9 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
       amax = NST == 0 ? max_nan(amax, other) : fmaxf(amax, other);
     }
     unsigned* rm = rowmax + rm_cur * R;
+    unsigned* rf = rowmax + (3 + rm_cur) * R;  // short order: the row held a NaN
     if (active && (lane & (seg - 1)) == 0) atomicMax(&rm[row_local], __float_as_uint(amax));
+    if (!EXACT && NST != 0 && active && has_nan) atomicOr(&rf[row_local], 1u);
     __syncthreads();
     if (abort_flag) break;
 
@@ -461,7 +614,10 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
     // The slot after next was last read before the previous barrier and is
     // next written after the following one.
     const int rm_clear = rm_cur == 0 ? 2 : rm_cur - 1;
-    if (tid < R) rowmax[rm_clear * R + tid] = 0u;
+    if (tid < R) {
+      rowmax[rm_clear * R + tid] = 0u;
+      rowmax[(3 + rm_clear) * R + tid] = 0u;
+    }
 
     const int row = batch * R + row_local;
     if (NST == 0 && active && row < M) {
@@ -497,32 +653,46 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
         }
       }
     } else if (NST != 0 && active && row < M) {
-      const float am = __uint_as_float(rm[row_local]);
+      const unsigned am_bits = rm[row_local];
+      const float am = __uint_as_float(am_bits);
       const float sc = fmaxf(__fdiv_rn(am, kQmaxRoot), 1e-30f);
       if (chunk == 0) sout[row] = sc;
       const float inv = __fdiv_rn(1.0f, __fmul_rn(sc, kRoot));
       const float2 inv2 = make_float2(inv, inv);
-      int8_t* qp = qout + size_t(row) * size_t(K) + code_off;
-      if (NST == 4) {
+      if (EXACT) {
+        int8_t* qp = qout + size_t(row) * size_t(K) + code_off;
+        if (NST == 4) {
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          uint32_t wd[4];
+          for (int r = 0; r < 4; ++r) {
+            uint32_t wd[4];
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            wd[k] = pack4(code_bits2(w2[r][2 * k], inv2), code_bits2(w2[r][2 * k + 1], inv2));
-          *reinterpret_cast<uint4*>(qp + r * 64) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            for (int k = 0; k < 4; ++k)
+              wd[k] = pack4(code_bits2(w2[r][2 * k], inv2), code_bits2(w2[r][2 * k + 1], inv2));
+            *reinterpret_cast<uint4*>(qp + r * 64) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t wd[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int i = 8 * c + 2 * k;  // pair index of value 16c + 4k
+              wd[k] = pack4(code_bits2(vp[i], inv2), code_bits2(vp[i + 1], inv2));
+            }
+            *reinterpret_cast<uint4*>(qp + c * 16) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+          }
         }
       } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t wd[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int i = 8 * c + 2 * k;  // pair index of value 16c + 4k
-            wd[k] = pack4(code_bits2(vp[i], inv2), code_bits2(vp[i + 1], inv2));
-          }
-          *reinterpret_cast<uint4*>(qp + c * 16) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-        }
+        // Positions hold outputs in reverse (see bfly4x2_short).  NST == 4:
+        // this thread's block (column block qd of input c) holds outputs of
+        // block 3 - qd of output quarter 3 - c, each 16 reversed.  NST < 4:
+        // position p of the line holds output p ^ (G - 1).
+        int8_t* qp = qout + size_t(row) * size_t(K) + code_off_short;
+        const bool finite_row = am_bits < 0x7f800000u && rf[row_local] == 0u;
+        if (finite_row)
+          store_codes_short<NST, true>(qp, vp, w2, inv2);
+        else
+          store_codes_short<NST, false>(qp, vp, w2, inv2);
       }
     }
     rm_cur = rm_cur == 2 ? 0 : rm_cur + 1;

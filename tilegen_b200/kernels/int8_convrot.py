@@ -1,15 +1,22 @@
 """ConvRot activation quantiser (API of tilegen/kernels/int8_convrot.py).
 
 ``quantize_convrot_fht`` / ``quantize_convrot_native`` run the prebuilt sm_100a
-rotate+quant kernel (``tg_rotate_quant``), which replaces the reference's NVRTC
-kernel (int8_convrot.py:41-230): same arithmetic, bit-identical codes and
-scales for fp16 input, no JIT and no per-K module cache.  Differences, by
-design:
+rotate+quant kernel (``tg_quantize_act``), which replaces the reference's NVRTC
+kernel (int8_convrot.py:41-230): the same rotation, row absmax, scale and
+rounding, no JIT and no per-K module cache.  Differences, by design:
 
 * bf16 input is read directly instead of being cast to fp16 first
   (int8_convrot.py:204-206), which matches ``_eager_quantize(x.float(), G)``.
-* groups 4, 16 and 64 are served natively too (the reference kernel only does
-  256); 128 is rejected as in the reference (not a power of four).
+* ``quantize_convrot_native`` also serves groups 4, 16 and 64 (the reference
+  kernel only does 256); 128 is rejected as in the reference (not a power of
+  four).  ``can_use_fht`` keeps the reference's rule (group 256 only), so
+  ``quantize_convrot`` sends the other groups to the eager path, in ``x``'s
+  dtype, exactly as the reference does.
+* the rotation's fp32 sums run in a shorter order than the reference
+  kernel's (``ops.ROTATION_ORDERS``): codes can differ by one at rounding ties
+  (about 1e-6 of them), within the parity tolerance;
+  ``ops.rotate_quant(x, G, order="reference")`` gives the reference kernel's
+  bits.
 * the ``tilelang`` implementation choice (``TILEGEN_FHT_IMPL``) has no separate
   lowering here; the native kernel serves it.
 
@@ -69,7 +76,7 @@ def can_use_fht(x: torch.Tensor, group_size: int, min_k: int = 0) -> bool:
     """Whether the FHT kernel handles ``x`` (``min_k``: smallest K worth it; 0 = any)."""
     if not x.is_cuda or x.dtype not in (torch.float16, torch.bfloat16):
         return False
-    if group_size not in NATIVE_GROUP_SIZES or x.shape[-1] % 256:
+    if group_size != KERNEL_GROUP_SIZE or x.shape[-1] % 256:
         return False
     if x.shape[-1] < min_k:
         return False

@@ -26,6 +26,20 @@ _DTYPE_CODE = {
 _SUPPORTED_GROUPS = (4, 16, 64, 256)
 # input_act names (tilegen/comfyui/backend.py:174) the quantiser applies itself.
 FUSED_ACTS = {"gelu_tanh": _lib.TG_ACT_GELU_TANH, "gelu": _lib.TG_ACT_GELU}
+# Butterfly orders of the rotation.  "short" (the default): per radix-4
+# butterfly S = (a0 + a2) + (a1 + a3) and each output S - 2*a_i in one fma, and
+# the codes' rint(v * inv) in one fma for rows without inf/NaN -- codes differ
+# from the reference kernel's by one at rounding ties (about 1e-6 of them on
+# DiT-like activations; the parity tolerance allows 1e-3), scales by a few
+# ulps.  "reference": the reference kernel's left-to-right sums
+# (tilegen/kernels/int8_convrot.py:74-77), bit-identical to it.
+ROTATION_ORDERS = {"short": 0, "reference": _lib.TG_QUANT_REFERENCE_ORDER}
+
+
+def _order_flag(fn: str, order: str) -> int:
+    if order not in ROTATION_ORDERS:
+        raise ValueError(f"{fn}: order must be one of {sorted(ROTATION_ORDERS)}, got {order!r}")
+    return ROTATION_ORDERS[order]
 
 
 def _aligned(t: torch.Tensor) -> torch.Tensor:
@@ -51,13 +65,14 @@ def rotate_quant_max_k() -> int:
     return int(_lib.lib().tg_rotate_quant_max_k())
 
 
-def rotate_quant(x: torch.Tensor, group: int = 256):
+def rotate_quant(x: torch.Tensor, group: int = 256, order: str = "short"):
     """Group-Hadamard rotation + row-wise int8 quantisation of ``x [M, K]``.
 
     Returns ``(q int8 [M, K], scale fp32 [M])``.  ``x`` must be a CUDA fp16/bf16
     tensor, ``group`` one of 4/16/64/256 and ``K`` a multiple of 256 (at most
-    ``rotate_quant_max_k()``).
+    ``rotate_quant_max_k()``).  ``order``: a key of ``ROTATION_ORDERS``.
     """
+    flag = _order_flag("rotate_quant", order)
     if not isinstance(x, torch.Tensor) or not x.is_cuda:
         raise ValueError("rotate_quant: CUDA tensor required")
     if x.ndim != 2:
@@ -73,12 +88,12 @@ def rotate_quant(x: torch.Tensor, group: int = 256):
     q = torch.empty((m, k), dtype=torch.int8, device=x.device)
     s = torch.empty((m,), dtype=torch.float32, device=x.device)
     if m:
-        _call("tg_rotate_quant", x.device, x.data_ptr(), _DTYPE_CODE[x.dtype], m, k, int(group),
-              q.data_ptr(), s.data_ptr())
+        _call("tg_quantize_act", x.device, x.data_ptr(), _DTYPE_CODE[x.dtype], m, k, int(group),
+              _lib.TG_ACT_NONE | flag, q.data_ptr(), s.data_ptr())
     return q, s
 
 
-def quantize_act(x: torch.Tensor, group: int = 256, act: str | None = None):
+def quantize_act(x: torch.Tensor, group: int = 256, act: str | None = None, order: str = "short"):
     """``act`` applied to ``x [M, K]``, then rotate+quantise (``group`` 4..256) or,
     with ``group=1``, the rotation-free row-wise quantisation of
     tilegen/comfyui/backend.py:230-232.  One pass over ``x`` (``tg_quantize_act``).
@@ -86,8 +101,10 @@ def quantize_act(x: torch.Tensor, group: int = 256, act: str | None = None):
     ``act``: None/``"none"``, or a name in ``FUSED_ACTS``; the activation is what
     torch's ``F.gelu`` (``approximate="tanh"`` for ``gelu_tanh``) stores for an
     fp16/bf16 tensor.  Returns ``(q int8 [M, K], scale fp32 [M])``.  ``K`` must be
-    a multiple of 256 (of 64 for ``group=1``).
+    a multiple of 256 (of 64 for ``group=1``).  ``order``: a key of
+    ``ROTATION_ORDERS`` (the row-wise form has no rotation).
     """
+    flag = _order_flag("quantize_act", order)
     if not isinstance(x, torch.Tensor) or not x.is_cuda:
         raise ValueError("quantize_act: CUDA tensor required")
     if x.ndim != 2:
@@ -109,7 +126,7 @@ def quantize_act(x: torch.Tensor, group: int = 256, act: str | None = None):
     q = torch.empty((m, k), dtype=torch.int8, device=x.device)
     s = torch.empty((m,), dtype=torch.float32, device=x.device)
     if m:
-        _call("tg_quantize_act", x.device, x.data_ptr(), _DTYPE_CODE[x.dtype], m, k, int(group), code,
+        _call("tg_quantize_act", x.device, x.data_ptr(), _DTYPE_CODE[x.dtype], m, k, int(group), code | flag,
               q.data_ptr(), s.data_ptr())
     return q, s
 

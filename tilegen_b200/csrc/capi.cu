@@ -14,7 +14,6 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr int64_t kRotQuantMaxK = 32768;
-constexpr int kRotQuantRegs = 96;  // __maxnreg__ of rotquant_kernel
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -75,15 +74,57 @@ bool ensure_smem_attr(K kernel, int dev, uint32_t bytes, uint32_t* done_bytes) {
 }
 
 // ------------------------------------------------------------------ rotate+quant
-template <int NST, bool BF16, int ACT, bool EXACT>
-int launch_rotquant_t(const CUtensorMap& tm, const tg::RotQuantParams& p, int threads, uint32_t smem, int dev,
-                      int sms, cudaStream_t st) {
+// Dynamic shared memory of a launch: alignment slack, the ring of `stages`
+// slots, their mbarriers, and the row maxima and NaN flags ([3][R] each).
+uint32_t rotquant_smem(int stages, uint32_t stage_bytes, int R) {
+  return 1024u + uint32_t(stages) * stage_bytes + uint32_t(stages) * 8u + uint32_t(6 * R) * 4u;
+}
+
+constexpr uint32_t kSmemPerCtaMax = 232448u;  // 227 KB: the opt-in maximum of one CTA
+constexpr uint32_t kSmemPerSm = 233472u;      // 228 KB per SM, 1 KB of it reserved per resident CTA
+
+// CTAs per SM that a rotquant variant's registers allow (with the shallowest
+// ring), and the deepest ring (2 to 4 slots) that that many CTAs fit.
+template <int NST, bool BF16, int ACT, bool EXACT, int REGS>
+bool rotquant_shape(int dev, int threads, uint32_t stage_bytes, int R, int* occ_out, int* stages_out) {
   static uint32_t attr_done[kMaxDevices];
-  auto kern = tg::rotquant_kernel<NST, BF16, ACT, EXACT>;
-  if (!ensure_smem_attr(kern, dev, smem, attr_done)) return TG_ERR_CUDA;
+  static uint32_t static_smem = ~0u;
+  // (occ | stages << 8) per device, CTA width in warps and rows per batch; 0 = not known yet.
+  static int known[kMaxDevices][17][9];
+  const int tw = threads / 32;
+  if (tw <= 16 && R <= 8 && known[dev][tw][R] != 0) {
+    *occ_out = known[dev][tw][R] & 0xff;
+    *stages_out = known[dev][tw][R] >> 8;
+    return true;
+  }
+  auto kern = tg::rotquant_kernel<NST, BF16, ACT, EXACT, REGS>;
+  if (static_smem == ~0u) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return false;
+    static_smem = uint32_t(fa.sharedSizeBytes);
+  }
+  const uint32_t dyn_max = kSmemPerCtaMax - static_smem;  // static + dynamic <= the per-CTA maximum
+  if (!ensure_smem_attr(kern, dev, dyn_max, attr_done)) return false;
   int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem) != cudaSuccess || occ < 1)
-    return TG_ERR_CUDA;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, rotquant_smem(2, stage_bytes, R)) !=
+          cudaSuccess ||
+      occ < 1)
+    return false;
+  int stages = 4;
+  while (stages > 2 && (rotquant_smem(stages, stage_bytes, R) > dyn_max ||
+                        uint64_t(occ) * (rotquant_smem(stages, stage_bytes, R) + static_smem + 1024u) > kSmemPerSm))
+    --stages;
+  *occ_out = occ;
+  *stages_out = stages;
+  if (tw <= 16 && R <= 8) known[dev][tw][R] = occ | (stages << 8);
+  return true;
+}
+
+template <int NST, bool BF16, int ACT, bool EXACT, int REGS>
+int launch_rotquant_t(const CUtensorMap& tm, tg::RotQuantParams p, int threads, int occ, int dev, int sms,
+                      cudaStream_t st) {
+  auto kern = tg::rotquant_kernel<NST, BF16, ACT, EXACT, REGS>;
+  const uint32_t smem = rotquant_smem(p.stages, p.stage_bytes, p.rows_per_batch);
   const int64_t grid64 = std::min<int64_t>(p.nbatches, int64_t(sms) * occ);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -99,14 +140,39 @@ int launch_rotquant_t(const CUtensorMap& tm, const tg::RotQuantParams& p, int th
   return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
 }
 
+// The register budget.  96 registers a thread by default; the hot form (G=256,
+// short order, no activation) also has an 80-register build, taken when it
+// keeps more warps resident: a CTA of seven warps (K=13824: 216 lines a row)
+// fits twice per SM at 96 registers (five warps' registers per SM
+// sub-partition) but three times at 80.
+template <int NST, bool BF16, int ACT, bool EXACT>
+int launch_rotquant_regs(const CUtensorMap& tm, tg::RotQuantParams p, int threads, int dev, int sms,
+                         cudaStream_t st) {
+  int occ = 0, stages = 0;
+  if (!rotquant_shape<NST, BF16, ACT, EXACT, 96>(dev, threads, p.stage_bytes, p.rows_per_batch, &occ, &stages))
+    return TG_ERR_CUDA;
+  if constexpr (NST == 4 && ACT == tg::kActNone && !EXACT) {
+    int occ80 = 0, stages80 = 0;
+    if (!rotquant_shape<NST, BF16, ACT, EXACT, 80>(dev, threads, p.stage_bytes, p.rows_per_batch, &occ80,
+                                                   &stages80))
+      return TG_ERR_CUDA;
+    if (occ80 > occ) {
+      p.stages = stages80;
+      return launch_rotquant_t<NST, BF16, ACT, EXACT, 80>(tm, p, threads, occ80, dev, sms, st);
+    }
+  }
+  p.stages = stages;
+  return launch_rotquant_t<NST, BF16, ACT, EXACT, 96>(tm, p, threads, occ, dev, sms, st);
+}
+
 template <int NST, bool BF16, bool EXACT>
-int launch_rotquant_act(int act, const CUtensorMap& tm, const tg::RotQuantParams& p, int threads, uint32_t smem,
-                        int dev, int sms, cudaStream_t st) {
+int launch_rotquant_act(int act, const CUtensorMap& tm, const tg::RotQuantParams& p, int threads, int dev, int sms,
+                        cudaStream_t st) {
   switch (act) {
     case TG_ACT_GELU_TANH:
-      return launch_rotquant_t<NST, BF16, tg::kActGeluTanh, EXACT>(tm, p, threads, smem, dev, sms, st);
-    case TG_ACT_GELU: return launch_rotquant_t<NST, BF16, tg::kActGelu, EXACT>(tm, p, threads, smem, dev, sms, st);
-    default: return launch_rotquant_t<NST, BF16, tg::kActNone, EXACT>(tm, p, threads, smem, dev, sms, st);
+      return launch_rotquant_regs<NST, BF16, tg::kActGeluTanh, EXACT>(tm, p, threads, dev, sms, st);
+    case TG_ACT_GELU: return launch_rotquant_regs<NST, BF16, tg::kActGelu, EXACT>(tm, p, threads, dev, sms, st);
+    default: return launch_rotquant_regs<NST, BF16, tg::kActNone, EXACT>(tm, p, threads, dev, sms, st);
   }
 }
 
@@ -114,12 +180,12 @@ int launch_rotquant_act(int act, const CUtensorMap& tm, const tg::RotQuantParams
 // short one (the default).  The rotation-free form has no butterflies.
 template <int NST, bool BF16>
 int launch_rotquant_order(bool exact, int act, const CUtensorMap& tm, const tg::RotQuantParams& p, int threads,
-                          uint32_t smem, int dev, int sms, cudaStream_t st) {
+                          int dev, int sms, cudaStream_t st) {
   if constexpr (NST == 0) {
-    return launch_rotquant_act<NST, BF16, true>(act, tm, p, threads, smem, dev, sms, st);
+    return launch_rotquant_act<NST, BF16, true>(act, tm, p, threads, dev, sms, st);
   } else {
-    if (exact) return launch_rotquant_act<NST, BF16, true>(act, tm, p, threads, smem, dev, sms, st);
-    return launch_rotquant_act<NST, BF16, false>(act, tm, p, threads, smem, dev, sms, st);
+    if (exact) return launch_rotquant_act<NST, BF16, true>(act, tm, p, threads, dev, sms, st);
+    return launch_rotquant_act<NST, BF16, false>(act, tm, p, threads, dev, sms, st);
   }
 }
 
@@ -210,15 +276,9 @@ int tg_quantize_act(const void* x, int x_dtype, int64_t M, int64_t K, int group,
         break;
       }
   }
+  // The ring's depth (2 to 4 slots) is chosen at launch from the kernel's
+  // occupancy (launch_rotquant_regs).
   const uint32_t stage_bytes = uint32_t(threads) * 128u;
-  // Ring depth: as deep as possible (up to 4) while the CTAs that the register
-  // budget allows per SM (96 registers a thread) still fit in shared memory.
-  int ctas = 65536 / (threads * kRotQuantRegs);
-  ctas = ctas < 1 ? 1 : ctas;
-  const uint32_t per_cta = 232448u / uint32_t(ctas) - 2048u - 1024u - uint32_t(6 * R) * 4u;
-  int stages = int(per_cta / stage_bytes);
-  stages = stages < 2 ? 2 : (stages > 4 ? 4 : stages);
-  const uint32_t smem = 1024u + uint32_t(stages) * stage_bytes + uint32_t(stages) * 8u + uint32_t(6 * R) * 4u;
 
   int dev;
   DeviceInfo info;
@@ -240,24 +300,24 @@ int tg_quantize_act(const void* x, int x_dtype, int64_t M, int64_t K, int group,
   p.box_lines = box;
   p.boxes = active / box;
   p.nbatches = (M + R - 1) / R;
-  p.stages = stages;
+  p.stages = 2;
   p.stage_bytes = stage_bytes;
   p.seg = gcd_int(cpr, 32);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf = x_dtype == TG_DT_BF16;
-#define TG_RQ_CASE(N)                                                                                 \
-  case N:                                                                                             \
-    return bf ? launch_rotquant_order<N, true>(exact, act, tm, p, threads, smem, dev, info.sms, st) \
-              : launch_rotquant_order<N, false>(exact, act, tm, p, threads, smem, dev, info.sms, st);
+#define TG_RQ_CASE(N)                                                                           \
+  case N:                                                                                       \
+    return bf ? launch_rotquant_order<N, true>(exact, act, tm, p, threads, dev, info.sms, st) \
+              : launch_rotquant_order<N, false>(exact, act, tm, p, threads, dev, info.sms, st);
   switch (nst) {
     TG_RQ_CASE(0)
     TG_RQ_CASE(1)
     TG_RQ_CASE(2)
     TG_RQ_CASE(3)
     default:
-      return bf ? launch_rotquant_order<4, true>(exact, act, tm, p, threads, smem, dev, info.sms, st)
-                : launch_rotquant_order<4, false>(exact, act, tm, p, threads, smem, dev, info.sms, st);
+      return bf ? launch_rotquant_order<4, true>(exact, act, tm, p, threads, dev, info.sms, st)
+                : launch_rotquant_order<4, false>(exact, act, tm, p, threads, dev, info.sms, st);
   }
 #undef TG_RQ_CASE
 }

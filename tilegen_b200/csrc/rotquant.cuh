@@ -309,6 +309,23 @@ __device__ __forceinline__ uint32_t pack4_rev(uint2 a, uint2 b) {
   return pack4(make_uint2(b.y, b.x), make_uint2(a.y, a.x));
 }
 
+// The row scale max(am / (127 sqrt(G)), 1e-30) for a finite am >= 0, equal to
+// the IEEE quotient the reference divides (int8_convrot.py:95) without a
+// division: q = am * RN(1/d), the remainder am - q*d exact in one fma, and one
+// fma correction q + rem * RN(1/d) (Markstein's method, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990).  Checked against the division for every non-negative
+// finite fp32 and each d = 127 sqrt(G) of G = 4, 16, 64, 256; the quotients
+// that the correction can miss are subnormal, below the 1e-30 clamp.
+template <int NST>
+__device__ __forceinline__ float rot_scale(float am) {
+  constexpr float d = 127.0f * float(1 << NST);
+  constexpr float c = 1.0f / d;
+  const float q = __fmul_rn(am, c);
+  const float r = __fmaf_rn(-q, d, am);
+  return fmaxf(__fmaf_rn(r, c, q), 1e-30f);
+}
+
 template <bool FUSED>
 __device__ __forceinline__ uint2 codes2(float2 x, float2 inv2) {
   return FUSED ? code_bits2_fused(x, inv2) : code_bits2(x, inv2);
@@ -398,11 +415,10 @@ __device__ __forceinline__ uint32_t rowwise_codes4(float2 a, float2 b, float2 rc
   return __byte_perm(*reinterpret_cast<const uint32_t*>(&ha), *reinterpret_cast<const uint32_t*>(&hb), 0x6420);
 }
 
-template <int NST, bool BF16, int ACT, bool EXACT>
-__global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
+template <int NST, bool BF16, int ACT, bool EXACT, int REGS>
+__global__ void __maxnreg__(REGS) rotquant_kernel(const __grid_constant__ CUtensorMap tmx,
                                                        const RotQuantParams p) {
   constexpr float kRoot = float(1 << NST);               // sqrt(G)
-  constexpr float kQmaxRoot = 127.0f * float(1 << NST);  // 2032 for G = 256
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -482,6 +498,13 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
   const int code_off = NST == 4 ? (chunk >> 2) * 256 + (chunk & 3) * 16 : chunk * 64;
   // The short order's reversed positions put NST == 4's block at 3 - qd.
   const int code_off_short = NST == 4 ? (chunk >> 2) * 256 + (3 - (chunk & 3)) * 16 : chunk * 64;
+
+  // Row absmax across lanes: with 32 or more lines a row (K >= 2048) a warp
+  // holds parts of at most two rows (the row of its lane 0, and the next), so
+  // two warp-wide max reductions cover it; shorter rows use shuffles over
+  // segments of `seg` lanes.
+  const bool two_rows_per_warp = cpr >= 32;
+  const bool in_row0 = row_local == (warp * 32) / cpr;
 
   int s = 0;
   uint32_t parity = 0;
@@ -595,13 +618,22 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
     // ---- row absmax -----------------------------------------------------------
     // (NST == 0: a NaN wins; its sign bit is clear after fabsf, so its bit
     // pattern also wins the unsigned atomicMax below.)
-    for (int o = 1; o < seg; o <<= 1) {
-      const float other = __shfl_xor_sync(0xffffffffu, amax, o);
-      amax = NST == 0 ? max_nan(amax, other) : fmaxf(amax, other);
-    }
     unsigned* rm = rowmax + rm_cur * R;
     unsigned* rf = rowmax + (3 + rm_cur) * R;  // short order: the row held a NaN
-    if (active && (lane & (seg - 1)) == 0) atomicMax(&rm[row_local], __float_as_uint(amax));
+    if (two_rows_per_warp) {
+      // Non-negative floats order as their bit patterns: one warp-wide integer
+      // max per row, the other row's lanes and idle threads contributing 0.
+      const unsigned bits = active ? __float_as_uint(amax) : 0u;
+      const unsigned m0 = __reduce_max_sync(0xffffffffu, in_row0 ? bits : 0u);
+      const unsigned m1 = __reduce_max_sync(0xffffffffu, in_row0 ? 0u : bits);
+      if (active && (lane == 0 || chunk == 0)) atomicMax(&rm[row_local], in_row0 ? m0 : m1);
+    } else {
+      for (int o = 1; o < seg; o <<= 1) {
+        const float other = __shfl_xor_sync(0xffffffffu, amax, o);
+        amax = NST == 0 ? max_nan(amax, other) : fmaxf(amax, other);
+      }
+      if (active && (lane & (seg - 1)) == 0) atomicMax(&rm[row_local], __float_as_uint(amax));
+    }
     if (!EXACT && NST != 0 && active && has_nan) atomicOr(&rf[row_local], 1u);
     __syncthreads();
     if (abort_flag) break;
@@ -655,9 +687,9 @@ __global__ void __maxnreg__(96) rotquant_kernel(const __grid_constant__ CUtensor
     } else if (NST != 0 && active && row < M) {
       const unsigned am_bits = rm[row_local];
       const float am = __uint_as_float(am_bits);
-      const float sc = fmaxf(__fdiv_rn(am, kQmaxRoot), 1e-30f);
+      const float sc = am_bits < 0x7f800000u ? rot_scale<NST>(am) : am;  // inf stays inf
       if (chunk == 0) sout[row] = sc;
-      const float inv = __fdiv_rn(1.0f, __fmul_rn(sc, kRoot));
+      const float inv = __frcp_rn(__fmul_rn(sc, kRoot));  // correctly rounded: 1 / (sqrt(G) * scale)
       const float2 inv2 = make_float2(inv, inv);
       if (EXACT) {
         int8_t* qp = qout + size_t(row) * size_t(K) + code_off;

@@ -18,11 +18,15 @@ CUDA events on the launching stream.
 The JSON line also carries: the roofline of the dominant kernel (the GEMM,
 tensor-bound) and of the quantiser (HBM-bound), the cuBLAS bf16 F.linear time
 of the same shape and the speedup over it, an end-to-end number through the
-public API with host buffers, the CPU baseline (the oracle port on the host
-cores, a bounded sample), sampled SM clocks, and (N=1) the four DiT shapes.
+reference's plugin call (``tilegen.comfyui.backend.int8_linear``) with host
+buffers, the CPU baseline (the reference's own CPU path on the host cores,
+whole steps), sampled SM clocks, and (N=1) the four DiT shapes and the
+quantiser sweep.
 
-``--impl reference`` times the reference algorithm's CPU implementation (the
-oracle port, all host threads) on the same workload; rank 0 only.
+``--impl reference`` times the reference's own CPU path of the same linear
+(its eager rotate+quant on ``x.float()`` and its chunked GEMM on torch's CPU
+``_int_mm``, from the package installed in ``baseline/_ref``) on all host
+threads, one whole 4096-row linear per step; rank 0 only.
 """
 from __future__ import annotations
 
@@ -44,6 +48,7 @@ GROUP = 256
 SHAPE = ("qkv_proj", 5120, 15360)
 NOMINAL_INT8_TOPS = 4500.0
 PUBLISHED_QKV_US = 10550.0  # RTX 2080 Ti, tilegen FHT int8_convrot qkv_proj, README.md:9
+METRIC = "int8_convrot linear us (M=4096) & speedup vs bf16 cuBLAS; quantizer HBM GB/s"
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each
 # kernel on this workload, from an ncu capture on a B200.  The quantiser's 21 MB
 # of codes are still in L2 when it ends, so its traffic is below its algorithmic
@@ -138,43 +143,90 @@ def _setup_dist(args):
     return world, rank, local
 
 
-class CpuLinear:
-    """The reference algorithm on the host cores (the C oracle port, all threads).
+def _reference_cpu():
+    """The reference's own CPU path of the linear (BASELINE plan: its eager
+    rotate+quant on the fp32-upcast activations, tilegen/kernels/int8_convrot.py:289-302,
+    and its chunked GEMM + dequant on torch's CPU ``_int_mm``,
+    tilegen/quant/int8_ops.py:22-70; the weight quantised offline by its
+    quantize_convrot_weight, weight.py:14-39).
 
-    The weight is quantised once at set-up (it is offline in the reference too);
-    ``time_rows(m)`` times rotate+quant and GEMM+dequant of ``m`` activation rows.
+    Imported from the reference package installed in ``baseline/_ref`` (loaded
+    under the name ``tilegen_ref``, since ``tilegen`` here is this repository's
+    alias package): kind "reference".  Without that install, this repository's
+    torch restatement of the same functions on CPU tensors (the eager path and
+    ``_int_mm`` chunks of ``tilegen_b200``): kind "port".
     """
+    import importlib
+    import importlib.util
+
+    root = os.path.join(HERE, "baseline", "_ref", "tilegen")
+    if os.path.isfile(os.path.join(root, "__init__.py")):
+        if "tilegen_ref" not in sys.modules:
+            spec = importlib.util.spec_from_file_location("tilegen_ref", os.path.join(root, "__init__.py"),
+                                                          submodule_search_locations=[root])
+            mod = importlib.util.module_from_spec(spec)
+            sys.modules["tilegen_ref"] = mod
+            spec.loader.exec_module(mod)
+        conv = importlib.import_module("tilegen_ref.kernels.int8_convrot")
+        ops_ = importlib.import_module("tilegen_ref.quant.int8_ops")
+        weight = importlib.import_module("tilegen_ref.quant.weight")
+        return ("reference", conv._eager_quantize, ops_.int8_matmul_dequant_chunked,
+                weight.quantize_convrot_weight, "baseline/_ref (the reference package, unmodified)")
+    from tilegen_b200.kernels.int8_convrot import _eager_quantize
+    from tilegen_b200.quant.int8_ops import int8_matmul_dequant_chunked
+    from tilegen_b200.quant.weight import quantize_convrot_weight
+
+    return ("port", _eager_quantize, int8_matmul_dequant_chunked, quantize_convrot_weight,
+            "tilegen_b200's torch restatement on CPU tensors (baseline/_ref not installed)")
+
+
+class CpuLinear:
+    """The whole 4096-row linear on the host cores through the reference's CPU path
+    (``_reference_cpu``), all host threads; the weight is quantised once at set-up
+    (offline in the reference too)."""
 
     def __init__(self, k: int, n: int):
         import torch
 
-        import oracle
         from tilegen_b200.synthetic import gaussian_weight, outlier_activations
 
-        self.oracle = oracle
-        oracle.set_num_threads(os.cpu_count() or 1)
-        self.x = outlier_activations(M_PER_RANK, k, seed=0, dtype=torch.float16).view(torch.int16).numpy()
-        self.wq, self.ws = oracle.rotate_quant(gaussian_weight(n, k, seed=0).numpy(), "float32", GROUP)
-        self.threads = oracle.num_threads()
+        self.kind, self.quant, self.gemm, wquant, self.source = _reference_cpu()
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.threads = torch.get_num_threads()
+        self.x = outlier_activations(M_PER_RANK, k, seed=0, dtype=torch.float16)
+        self.wq, self.ws = wquant(gaussian_weight(n, k, seed=1000), GROUP)
 
-    def time_rows(self, m: int) -> float:
+    def step(self) -> float:
+        """Seconds for one linear: rotate+quant of x.float(), then GEMM + dequant to fp16."""
+        import torch
+
         t0 = time.perf_counter()
-        xq, xs = self.oracle.rotate_quant(self.x[:m], "float16", GROUP)
-        self.oracle.int8_gemm_dequant(xq, xs, self.wq, self.ws, None, "float16")
+        xq, xs = self.quant(self.x.float(), GROUP)
+        self.gemm(xq, xs, self.wq, self.ws, None, torch.float16)
         return time.perf_counter() - t0
 
-    def rows_for(self, seconds: float) -> int:
-        """Row count whose sample takes about ``seconds`` (at least 8, at most all)."""
-        t8 = self.time_rows(8)
-        return int(max(8, min(M_PER_RANK, 8 * seconds / max(t8, 1e-4))))
+    def sample(self) -> str:
+        return (f"whole {M_PER_RANK}-row steps of the workload: {self.source}: _eager_quantize(x.float(), {GROUP}) "
+                f"then int8_matmul_dequant_chunked (CPU torch._int_mm, 256 MiB chunks) to fp16")
 
 
-def _cpu_baseline_us(k, n, budget_s=10.0):
-    """Oracle time for one full 4096-row linear, scaled from a bounded row sample."""
+def _cpu_baseline(k, n, budget_s=15.0):
+    """Mean seconds per linear over whole steps run for about ``budget_s`` (at least 2)."""
     cpu = CpuLinear(k, n)
-    m = cpu.rows_for(budget_s)
-    dt = cpu.time_rows(m)
-    return dt / m * M_PER_RANK * 1e6, cpu.threads, f"{m} of {M_PER_RANK} rows (rotate+quant and GEMM+dequant), scaled"
+    cpu.step()  # warm-up: thread pool, allocator
+    times, t_end = [], time.perf_counter() + budget_s
+    while len(times) < 2 or time.perf_counter() < t_end:
+        times.append(cpu.step())
+    return statistics.mean(times), cpu, len(times)
+
+
+def _config(world: int) -> dict:
+    """The workload dict both arms print."""
+    name, k, n = SHAPE
+    return {"workload": _workload_desc(), "M_per_gpu": M_PER_RANK, "K": k, "N": n, "group": GROUP,
+            "parallelism": f"rows x {world} (no collective)",
+            "l2": "flushed before every timed GPU step: 256 MiB write, then a 256 MiB read of another "
+                  "buffer so the write's dirty lines are written back before the step"}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -185,23 +237,19 @@ def run_reference(args):
         return
     name, k, n = SHAPE
     cpu = CpuLinear(k, n)
-    # every step times the same bounded row sample; the whole run stays near 90 s
-    m = cpu.rows_for(90.0 / max(1, args.steps + args.warmup))
     for _ in range(args.warmup):
-        cpu.time_rows(m)
-    per_step = [cpu.time_rows(m) / m * M_PER_RANK * 1e6 for _ in range(args.steps)]
-    thr = cpu.threads
-    sample = f"{m} of {M_PER_RANK} rows per step (rotate+quant and GEMM+dequant), scaled to {M_PER_RANK}"
+        cpu.step()
+    per_step = [cpu.step() * 1e6 for _ in range(args.steps)]
     value = statistics.mean(per_step)
     line = {
-        "metric": "int8_convrot linear us (M=4096) & speedup vs bf16 cuBLAS; quantizer HBM GB/s",
-        "value": value, "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": value / 1e3, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "metric": METRIC,
+        "value": round(value, 1), "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(value / 1e3, 3), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8", "data": "synthetic", "impl": "reference",
-        "config": {"workload": _workload_desc(), "M": M_PER_RANK, "K": k, "N": n, "group": GROUP,
-                   "parallelism": "rank 0 host cores"},
-        "cpu_baseline": {"value": value, "unit": "us", "cores": thr, "kind": "port", "sample": sample},
-        "e2e": {"value": value, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": _config(world),
+        "cpu_baseline": {"value": round(value, 1), "unit": "us", "cores": cpu.threads, "kind": cpu.kind,
+                         "sample": cpu.sample()},
+        "e2e": {"value": round(value, 1), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -596,16 +644,26 @@ def run_tilegen(args):
                               "gemm_us": round(statistics.mean(tg) * 1e3, 2), "clocks": clocks}), flush=True)
         return
 
-    # ---- end to end through the public API, host buffers, copies timed ----
-    # The host-buffer linear (tilegen_b200.streaming.int8_linear_host: row chunks,
-    # H2D / kernels / D2H overlapped on three streams, captured once and replayed
-    # as a CUDA graph), and for reference the same copies and calls issued one
-    # after another on one stream.
+    # ---- end to end with host buffers, copies timed ----
+    # Headline: the reference-facing plugin call, tilegen.comfyui.backend.int8_linear
+    # (what comfy_kitchen's registry dispatches to), between a pinned host->device
+    # copy of x and a device->host copy of the output, one stream.  Also: the
+    # same through the quantiser and GEMM API calls, and this repository's
+    # host-buffer linear (tilegen_b200.streaming.int8_linear_host: row chunks with
+    # H2D / kernels / D2H overlapped on three streams, replayed as one CUDA graph).
+    from tilegen.comfyui import backend as plugin
     from tilegen_b200.streaming import int8_linear_host
 
     x_host = x.cpu().pin_memory()
     out_host = torch.empty((m, n), dtype=torch.float16).pin_memory()
     x_dev = torch.empty_like(x)
+
+    def e2e_plugin_step(e):
+        e[0].record(stream)
+        x_dev.copy_(x_host, non_blocking=True)
+        y = plugin.int8_linear(x_dev, wq, ws, None, torch.float16, convrot=True, convrot_groupsize=GROUP)
+        out_host.copy_(y, non_blocking=True)
+        e[1].record(stream)
 
     def e2e_step(e):
         e[0].record(stream)
@@ -631,12 +689,15 @@ def run_tilegen(args):
             dist.all_reduce(tot, op=dist.ReduceOp.MAX)
         return float(tot.item()) * 1e3 / (world * len(te))
 
+    e2e_plugin_us = e2e_time(e2e_plugin_step)
+    plugin_out = out_host.clone()
     e2e_us = e2e_time(e2e_step)
     e2e_serial_us = e2e_time(e2e_serial_step)
     ref_out = out_host.clone()
     e2e_step([torch.cuda.Event(enable_timing=True) for _ in range(2)])
     torch.cuda.synchronize()
-    e2e_bitexact = bool(torch.equal(out_host.view(torch.int16), ref_out.view(torch.int16)))
+    e2e_bitexact = bool(torch.equal(out_host.view(torch.int16), ref_out.view(torch.int16))
+                        and torch.equal(plugin_out.view(torch.int16), ref_out.view(torch.int16)))
 
     # ---- comparators ----
     bf16_us = _bf16_linear_us(x, w, max(5, min(args.steps, 50)), flush, stream)
@@ -654,8 +715,9 @@ def run_tilegen(args):
     block = _dit_block_bf16(dev, flush, stream, world, rank)
     gather = _gather_table(dev, flush, stream, world, rank) if world > 1 else None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu_us, cores, sample = _cpu_baseline_us(k, n)
-        cpu = {"value": round(cpu_us, 1), "unit": "us", "cores": cores, "kind": "port", "sample": sample}
+        cpu_s, cl, nsteps = _cpu_baseline(k, n)
+        cpu = {"value": round(cpu_s * 1e6, 1), "unit": "us", "cores": cl.threads, "kind": cl.kind,
+               "sample": f"{nsteps} " + cl.sample()}
 
     if world > 1:
         if rank == 0:
@@ -673,17 +735,14 @@ def run_tilegen(args):
     int8_peak = 2.0 * peaks["bf16_tflops"]
     lin_us = value_us if world == 1 else (quant_ms + gemm_ms) * 1e3
     line = {
-        "metric": "int8_convrot linear us (M=4096) & speedup vs bf16 cuBLAS; quantizer HBM GB/s",
+        "metric": METRIC,
         "value": round(value_us, 3), "unit": "us", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": round(max_total_ms / args.steps, 5),
         "higher_is_better": False, "scaling": "weak",
         "vs_baseline": round(value_us / PUBLISHED_QKV_US, 5),
         "vs_baseline_ref": "tilegen FHT int8_convrot qkv_proj on RTX 2080 Ti, 10.55 ms (README.md:9)",
         "dtype": "int8", "data": "synthetic",
-        "config": {"workload": _workload_desc(), "M_per_gpu": m, "K": k, "N": n, "group": GROUP,
-                   "parallelism": f"rows x {world} (no collective)",
-                   "l2": "flushed before every timed step: 256 MiB write, then a 256 MiB read of another "
-                         "buffer so the write's dirty lines are written back before the step"},
+        "config": _config(world),
         "speedup_vs_bf16_cublas": round(bf16_us / lin_us, 3), "bf16_cublas_us": round(bf16_us, 2),
         "quant_us": round(quant_ms * 1e3, 2), "gemm_us": round(gemm_ms * 1e3, 2),
         "kernel_split_note": "quant_us/gemm_us: each kernel timed alone (event between them); value: both back to back",
@@ -697,15 +756,18 @@ def run_tilegen(args):
                            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(quant_gbs / peaks["hbm_gbs"], 4),
                            "peak_source": peak_kind, "algorithmic_bytes_per_launch": quant_bytes,
                            "traffic": QUANT_TRAFFIC_BYTES},
-        "e2e": {"value": round(e2e_us, 2), "unit": "us", "h2d_bytes_per_step": x.numel() * 2,
+        "e2e": {"value": round(e2e_plugin_us, 2), "unit": "us", "h2d_bytes_per_step": x.numel() * 2,
                 "d2h_bytes_per_step": m * n * 2,
-                "path": "pinned host x -> tilegen_b200.streaming.int8_linear_host(graph=True) (chunks of 256, 512, "
-                        "then 1024 rows: H2D, rotate+quant + GEMM, D2H on three streams, replayed as one CUDA "
-                        "graph) -> pinned host out",
-                "serial_us": round(e2e_serial_us, 2),
-                "serial_path": "one stream: H2D of x, tilegen.kernels.quantize_convrot, "
-                               "tilegen.quant.int8_matmul_dequant_chunked, D2H of the output",
-                "bit_identical_to_serial": e2e_bitexact},
+                "path": "one stream: pinned host x -> device, tilegen.comfyui.backend.int8_linear(convrot=True) "
+                        "(the reference's plugin call), output -> pinned host",
+                "api_calls_us": round(e2e_serial_us, 2),
+                "api_calls_path": "one stream: H2D of x, tilegen.kernels.quantize_convrot, "
+                                  "tilegen.quant.int8_matmul_dequant_chunked, D2H of the output",
+                "host_linear_us": round(e2e_us, 2),
+                "host_linear_path": "pinned host x -> tilegen_b200.streaming.int8_linear_host(graph=True) (chunks "
+                                    "of 256, 512, then 1024 rows: H2D, rotate+quant + GEMM, D2H on three streams, "
+                                    "replayed as one CUDA graph) -> pinned host out",
+                "bit_identical_across_paths": e2e_bitexact},
         "gpu_launches": 2 * args.steps,  # rotquant_kernel + gemm_i8_dequant_kernel per step (timed region)
         "clocks": clocks,
         "device_status": status,

@@ -171,9 +171,11 @@ int tg_int8_gemm_dequant_splitk_config(int64_t M, int64_t N, int64_t K, int out_
  * Arguments and result as tg_int8_gemm_dequant_splitk without the workspace;
  * TG_ERR_UNSUPPORTED unless M <= 64, N <= 65536 and M * N <= 1048576.
  * The first call on a device looks up the array's device address (set-up, once
- * per device); make that first call before any stream capture.  Each call
- * zeroes the part of the array it uses (a memset on `stream`) before the
- * kernel.  All calls share the one array, so calls that overlap on the GPU
+ * per device); make that first call before any stream capture.  When the
+ * kernel sums through the array (tg_int8_gemm_dequant_splitk_config reports
+ * cluster == 0), the call first zeroes the part of the array it uses (a memset
+ * on `stream`); the cluster form sums in shared memory and leaves the array
+ * alone.  All calls share the one array, so calls that overlap on the GPU
  * (different streams, or concurrent host threads) race and corrupt each
  * other's results: serialise them.
  */

@@ -1,25 +1,27 @@
 """The bench's reference arm on the CPU: the JSON line the driver reads.
 
-The arm times the C oracle (the reference algorithm on the host cores) on a
-bounded row sample; here the sample is cut to 8 rows so the test is quick, and
-the line is checked against the bench contract.
+The arm times the reference's own CPU path of the linear (its eager
+rotate+quant and its chunked torch._int_mm GEMM, from the package installed in
+baseline/_ref, else this repository's torch restatement of the same functions),
+one whole 4096-row linear per step; the line is checked against the bench
+contract.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import os
 
 import bench
 
 
 def _args(**kw):
-    base = dict(steps=2, warmup=1, gpus=1, impl="reference", no_cpu=False, quick=False)
+    base = dict(steps=1, warmup=0, gpus=1, impl="reference", no_cpu=False, quick=False)
     base.update(kw)
     return argparse.Namespace(**base)
 
 
 def test_reference_arm_prints_the_contract_line(monkeypatch, capsys):
-    monkeypatch.setattr(bench.CpuLinear, "rows_for", lambda self, seconds: 8)
     monkeypatch.setenv("WORLD_SIZE", "1")
     monkeypatch.setenv("RANK", "0")
     bench.run_reference(_args())
@@ -28,11 +30,13 @@ def test_reference_arm_prints_the_contract_line(monkeypatch, capsys):
                 "scaling", "vs_baseline", "dtype", "data", "config", "impl", "cpu_baseline", "e2e"):
         assert key in line, key
     assert line["impl"] == "reference" and line["unit"] == "us" and line["higher_is_better"] is False
-    assert line["steps"] == 2 and line["warmup"] == 1 and line["value"] > 0
-    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
-    assert line["cpu_baseline"]["value"] == line["value"] and "8 of 4096 rows" in line["cpu_baseline"]["sample"]
+    assert line["steps"] == 1 and line["warmup"] == 0 and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] in ("reference", "port") and line["cpu_baseline"]["cores"] >= 1
+    assert line["cpu_baseline"]["value"] == line["value"] and "4096-row steps" in line["cpu_baseline"]["sample"]
     assert line["e2e"] == {"value": line["value"], "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
-    assert line["config"]["M"] == 4096 and line["config"]["K"] == 5120 and line["config"]["N"] == 15360
+    # the tilegen arm prints the same dict (bench._config) for the same N
+    assert line["config"] == bench._config(1)
+    assert line["metric"] == bench.METRIC
 
 
 def test_reference_arm_runs_on_rank_zero_only(monkeypatch, capsys):
@@ -40,3 +44,14 @@ def test_reference_arm_runs_on_rank_zero_only(monkeypatch, capsys):
     monkeypatch.setenv("RANK", "1")
     bench.run_reference(_args())
     assert capsys.readouterr().out == ""
+
+
+def test_reference_cpu_path_is_the_installed_reference_when_present():
+    kind, quant, gemm, wquant, source = bench._reference_cpu()
+    installed = os.path.isfile(os.path.join(bench.HERE, "baseline", "_ref", "tilegen", "__init__.py"))
+    assert kind == ("reference" if installed else "port")
+    if installed:
+        # loaded from baseline/_ref under its own name, not this repository's alias package
+        assert os.path.realpath(quant.__code__.co_filename).startswith(
+            os.path.realpath(os.path.join(bench.HERE, "baseline", "_ref")))
+        assert quant.__module__ == "tilegen_ref.kernels.int8_convrot"

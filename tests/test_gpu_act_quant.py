@@ -212,3 +212,30 @@ def test_int8_linear_input_act_equals_reference_composition(cuda, fake_kitchen, 
     torch.cuda.synchronize()
     assert y.shape == ref.shape
     assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+
+
+def test_registry_rule_on_cuda_inputs(cuda, fake_kitchen, monkeypatch):
+    """The selective backend's call rule (the reference's rule order, backend.py:129-163):
+    group 256 only, K >= TILEGEN_FHT_MIN_K in auto mode (0 in fht mode), K within the
+    kernel's maximum, shapes that failed before refused; everything else accepted."""
+    from tilegen_b200 import ops
+    from tilegen_b200.comfyui import backend
+
+    def rule(x, group=256):
+        return backend._fht_applicable({"x": x, "weight": torch.zeros(8, x.shape[-1], dtype=torch.int8),
+                                        "convrot": True, "convrot_groupsize": group})
+
+    x = torch.zeros(4, 5120, dtype=torch.float16, device=cuda)
+    monkeypatch.setenv("TILEGEN_CONVROT_BACKEND", "auto")
+    monkeypatch.delenv("TILEGEN_FHT_MIN_K", raising=False)
+    assert rule(x).success                                         # Blackwell: min K 0
+    assert rule(x, 64).failed_param == "convrot_groupsize"       # other groups: eager, in x's dtype
+    assert rule(x.float()).failed_param == "x"                    # fp32: not a kernel input
+    monkeypatch.setenv("TILEGEN_FHT_MIN_K", "8192")
+    assert rule(x).failed_param == "x"                            # auto: below the threshold
+    monkeypatch.setenv("TILEGEN_CONVROT_BACKEND", "fht")
+    assert rule(x).success                                        # fht: no threshold
+    big = torch.zeros(1, ops.rotate_quant_max_k() + 256, dtype=torch.float16, device=cuda)
+    assert rule(big).failed_param == "x"
+    monkeypatch.setattr(backend, "_FAILED_FHT_SHAPES", {(4, 5120, torch.float16, cuda.index or 0)})
+    assert rule(x).failed_param == "x"

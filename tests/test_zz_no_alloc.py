@@ -4,10 +4,12 @@ Some callers cannot allocate device memory at all -- a plugin inside a host
 application that hands out all GPU memory through its own allocator, or a
 serving process that reserved its memory up front -- so this variant of the
 small-M GEMM keeps its scratch in a fixed array inside the library instead of
-taking a workspace.  The test calls it through the C ABI twice in a row (with
-different shapes, so the second call also shows the array holds nothing over
-from the first) and requires the same bits as the library's regular GEMM entry
-point on the same inputs; it also checks the size limits are refused cleanly.
+taking a workspace.  The test calls it through the C ABI on shapes whose K is
+split more ways than a cluster holds, so the partial sums really go through the
+library's array: twice in a row on one shape, then on a smaller one that reuses
+the start of the array, each time requiring the same bits as the library's
+regular GEMM entry point and as the oracle; it also checks that the size limits
+are refused cleanly.
 
 This file is collected last on purpose: the variant shares one array per GPU,
 so it runs after every other test, and it must pass in a fresh process too.
@@ -20,7 +22,8 @@ import numpy as np
 import pytest
 import torch
 
-from tests._util import out_bits
+import oracle
+from tests._util import DT_NAME, out_bits
 from tilegen_b200 import _lib, ops
 
 pytestmark = pytest.mark.gpu
@@ -69,16 +72,32 @@ def _regular(case, out_dtype):
         ops.SPLITK_MAX_M = old
 
 
+_CODE = {torch.float32: _lib.TG_DT_F32, torch.float16: _lib.TG_DT_F16, torch.bfloat16: _lib.TG_DT_BF16}
+
+
+def _oracle(case, out_dtype):
+    xq, xs, wq, ws, bias = (t.cpu() for t in case)
+    return oracle.int8_gemm_dequant(xq.numpy(), xs.numpy(), wq.numpy(), ws.numpy(), bias.numpy(),
+                                    DT_NAME[out_dtype])
+
+
 def test_two_calls_in_a_row_match_the_regular_entry_point(cuda):
     f = _fn()
-    # The first call is the largest; the second uses a different part of the
-    # shared array with other shapes and must not see the first call's sums.
-    for m, n, k, out_dtype, seed in ((64, 4096, 3072, torch.bfloat16, 1), (9, 1280, 5120, torch.float16, 2)):
+    # K split 9 and 24 ways (more than a cluster's 8): the partial sums go
+    # through the shared array.  The first shape covers the larger part of it;
+    # the second reuses its start.  Outputs must be bit-identical to the
+    # regular entry point and to the oracle, on both calls of the first shape.
+    shapes = ((64, 3328, 5120, torch.bfloat16, 1), (64, 3328, 5120, torch.bfloat16, 1),
+              (9, 1280, 5120, torch.float16, 2))
+    for m, n, k, out_dtype, seed in shapes:
+        slices, cluster = _lib.splitk_config(m, n, k, _CODE[out_dtype], True)
+        assert cluster == 0 and slices > 8, (m, n, k, slices, cluster)
         case = _case(m, n, k, seed, cuda)
         got = _noalloc(f, case, out_dtype)
         ref = _regular(case, out_dtype)
         torch.cuda.synchronize()
         assert np.array_equal(out_bits(got), out_bits(ref)), f"M={m} N={n} K={k}"
+        assert np.array_equal(out_bits(got), _oracle(case, out_dtype)), f"M={m} N={n} K={k} vs oracle"
     assert _lib.device_status(0) == 0
 
 

@@ -1,21 +1,25 @@
 """Selective comfy_kitchen ConvRot backend (API of tilegen/comfyui/backend.py).
 
 ``install()`` registers a backend named ``tilegen`` ahead of comfy_kitchen's
-other backends for ``int8_linear``; its call rule ``_fht_applicable`` accepts
-only the ConvRot calls the sm_100a kernels serve, everything else falls
-through to the next backend.  An accepted call runs ``int8_linear``: the fused
-rotate+quant kernel on the activations, then the fused tcgen05 INT8 GEMM with
-the dequantisation in its epilogue.
+other backends for ``int8_linear``.  Its call rule ``_fht_applicable`` accepts
+only the ConvRot calls the sm_100a kernels serve; anything else falls through
+to the next backend.  An accepted call runs ``int8_linear``: the rotate+quant
+kernel on the activations (with a ``gelu``/``gelu_tanh`` input activation
+applied inside it), then the tcgen05 INT8 GEMM with the dequantisation in its
+epilogue.
 
-Environment (same names and meanings as the reference, backend.py:39-78):
+One decision function, ``kernel_refusal``, says whether the kernel serves an
+activation tensor and, if not, why; the registry rule, ``int8_linear`` and the
+standalone linear node all ask it, so they cannot disagree.
+
+Environment (the reference's names and meanings, backend.py:39-78):
 ``TILEGEN_CONVROT_BACKEND`` in {auto, fht, eager, off}; ``TILEGEN_FHT_MIN_K``
-(default: 0 on compute capability 10.x and newer, where the kernel wins at every
-K, 5120 on sm_75, 8192 elsewhere); ``TILEGEN_INT8_TEMP_MB`` (accepted; the fused
-GEMM needs no temporary); ``TILEGEN_DIAGNOSTICS``.
+(default: 0 on compute capability 10.x and newer, where the kernel is faster
+at every K; 5120 on sm_75; 8192 elsewhere); ``TILEGEN_INT8_TEMP_MB`` (accepted;
+the fused GEMM needs no temporary); ``TILEGEN_DIAGNOSTICS``.
 """
 from __future__ import annotations
 
-import functools
 import logging
 import os
 import sys
@@ -29,83 +33,128 @@ LOGGER = logging.getLogger("tilegen.backend")
 
 BACKEND_NAME = "tilegen"
 _INSTALLED = False
+# (rows, K, dtype, device index) of inputs the kernel raised for: later calls
+# of that shape go to the eager path without trying again.
 _FAILED_FHT_SHAPES: set[tuple] = set()
 _LOGGED_DECISIONS: set[tuple] = set()
 
+_MODES = ("off", "auto", "fht", "eager")
+_FALSE_WORDS = ("0", "false", "off", "no")
 
+
+# ---------------------------------------------------------------- settings
 def _mode() -> str:
-    value = os.environ.get("TILEGEN_CONVROT_BACKEND", "auto").strip().lower()
-    if value not in {"off", "auto", "fht", "eager"}:
-        LOGGER.warning("Unknown TILEGEN_CONVROT_BACKEND=%r; using auto", value)
-        return "auto"
-    return value
+    """TILEGEN_CONVROT_BACKEND, lower-cased; an unknown value reads as ``auto`` (logged)."""
+    raw = os.environ.get("TILEGEN_CONVROT_BACKEND", "auto")
+    mode = raw.strip().lower()
+    if mode in _MODES:
+        return mode
+    LOGGER.warning("Unknown TILEGEN_CONVROT_BACKEND=%r; using auto", raw)
+    return "auto"
 
 
 def _default_fht_min_k(device_index: int = 0) -> int:
-    """Per-device K threshold below which ``auto`` keeps the stock backends."""
+    """Smallest K at which ``auto`` uses the kernel when TILEGEN_FHT_MIN_K is unset."""
     try:
-        if torch.cuda.is_available():
-            cap = torch.cuda.get_device_capability(device_index)
-            if cap[0] >= 10:
-                return 0
-            if cap == (7, 5):
-                return 5120
+        major, minor = torch.cuda.get_device_capability(device_index) if torch.cuda.is_available() else (0, 0)
     except (AssertionError, RuntimeError):
-        pass
-    return 8192
+        major, minor = 0, 0
+    if major >= 10:
+        return 0  # Blackwell: the fused kernel beats the eager path at every K
+    return 5120 if (major, minor) == (7, 5) else 8192
 
 
 def _fht_min_k(device_index: int = 0) -> int:
-    value = os.environ.get("TILEGEN_FHT_MIN_K")
-    if value is None:
+    raw = os.environ.get("TILEGEN_FHT_MIN_K")
+    if raw is None:
         return _default_fht_min_k(device_index)
     try:
-        return max(0, int(value))
+        return max(0, int(raw))
     except ValueError:
-        default = _default_fht_min_k(device_index)
-        LOGGER.warning("Invalid TILEGEN_FHT_MIN_K=%r; using %d", value, default)
-        return default
+        fallback = _default_fht_min_k(device_index)
+        LOGGER.warning("Invalid TILEGEN_FHT_MIN_K=%r; using %d", raw, fallback)
+        return fallback
 
 
 def _diagnostics_enabled() -> bool:
-    return os.environ.get("TILEGEN_DIAGNOSTICS", "1").strip().lower() not in {"0", "false", "off", "no"}
+    return os.environ.get("TILEGEN_DIAGNOSTICS", "1").strip().lower() not in _FALSE_WORDS
+
+
+def _temp_bytes() -> int:
+    return max(16, int(os.environ.get("TILEGEN_INT8_TEMP_MB", "256"))) << 20
 
 
 def _log_decision(decision: str, reason: str, x, weight, group_size: int) -> None:
-    """Log each distinct (decision, reason, shape) once, when diagnostics are on."""
-    if not _diagnostics_enabled() or not isinstance(x, torch.Tensor) or x.ndim < 2:
+    """One warning per distinct (decision, reason, shape, dtype, group), if diagnostics are on."""
+    if not (_diagnostics_enabled() and isinstance(x, torch.Tensor) and x.ndim >= 2):
         return
     k = x.shape[-1]
-    m = x.numel() // max(1, k)
+    rows = x.numel() // max(1, k)
     n = weight.shape[0] if isinstance(weight, torch.Tensor) and weight.ndim == 2 else "?"
-    key = (decision, reason, m, k, n, x.dtype, group_size)
-    if key in _LOGGED_DECISIONS:
-        return
-    _LOGGED_DECISIONS.add(key)
-    LOGGER.warning("tilegen shape %s: M=%s K=%s N=%s dtype=%s group=%s reason=%s",
-                   decision, m, k, n, x.dtype, group_size, reason)
+    key = (decision, reason, rows, k, n, x.dtype, group_size)
+    if key not in _LOGGED_DECISIONS:
+        _LOGGED_DECISIONS.add(key)
+        LOGGER.warning("tilegen shape %s: M=%s K=%s N=%s dtype=%s group=%s reason=%s",
+                       decision, rows, k, n, x.dtype, group_size, reason)
 
 
-@functools.lru_cache(maxsize=16)
-def _hadamard(device_type: str, device_index: int, dtype: torch.dtype, size: int):
-    from ..kernels.hadamard import build_hadamard
+# ---------------------------------------------------------------- the decision
+def kernel_refusal(x: torch.Tensor, group_size: int, mode: str, min_k: int | None = None):
+    """``None`` when the rotate+quant kernel serves ``x`` in ``mode``, else
+    ``(param, message, log_reason)``: the ValidationResult failure to report and
+    the reason to log (``None``: not worth a log line).
 
-    device = torch.device(device_type, device_index) if device_type == "cuda" else torch.device(device_type)
-    return build_hadamard(size, device, dtype)
+    Checks, in order: mode; a CUDA fp16/bf16 tensor of two or more dims; group
+    256 and K a multiple of 256 (the reference kernel's rule; other groups take
+    the eager path in x's dtype, as in the reference); K at least ``min_k``
+    (``auto`` only; default TILEGEN_FHT_MIN_K); K at most the kernel's maximum;
+    the shape not one the kernel already failed on.
+    """
+    from ..kernels.int8_convrot import KERNEL_GROUP_SIZE
+    from ..ops import rotate_quant_max_k
+
+    if mode not in ("auto", "fht"):
+        return "__tilegen__", f"mode={mode}", f"mode={mode}"
+    if not (isinstance(x, torch.Tensor) and x.is_cuda and x.ndim >= 2):
+        return "x", "CUDA tensor with at least 2 dims required", None
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        return "x", "fp16/bf16 input required", None
+    k = x.shape[-1]
+    if group_size != KERNEL_GROUP_SIZE or k % KERNEL_GROUP_SIZE:
+        return "convrot_groupsize", "requires group=256 and K divisible by 256", "unsupported group/K"
+    if mode == "auto":
+        floor = _fht_min_k(x.device.index or 0) if min_k is None else min_k
+        if k < floor:
+            return "x", "K below TileGen threshold", f"K below min_k={floor}"
+    if k > rotate_quant_max_k():
+        return "x", "K above the kernel's maximum", "K above the kernel's maximum"
+    if (x.numel() // k, k, x.dtype, x.device.index) in _FAILED_FHT_SHAPES:
+        return "x", "FHT previously failed for this shape", "FHT previously failed"
+    return None
 
 
-def _eager_quantize_convrot(x: torch.Tensor, group_size: int):
-    """Pure-torch activation ConvRot quantisation (backend.py:105-112)."""
-    m, k = x.shape
-    h = _hadamard(x.device.type, x.device.index or 0, x.dtype, group_size)
-    rot = torch.matmul(x.reshape(m, k // group_size, group_size), h).reshape(m, k)
-    scale = (rot.abs().amax(dim=-1).float() / 127.0).clamp_min(1e-30)
-    q = torch.round(rot / scale[:, None].to(rot.dtype)).clamp(-128, 127).to(torch.int8)
-    return q, scale
+def _fht_applicable(kwargs: Mapping[str, object]):
+    """Registry call rule: accept only the ConvRot calls the kernels serve."""
+    from comfy_kitchen.constraints import ValidationResult
+
+    if not kwargs.get("convrot", False):
+        return ValidationResult.fail("convrot", "TileGen only handles ConvRot")
+    x, weight = kwargs.get("x"), kwargs.get("weight")
+    group_size = int(kwargs.get("convrot_groupsize", 256))
+    mode = _mode()
+    refusal = kernel_refusal(x, group_size, mode, min_k=0 if mode == "fht" else None)
+    if refusal is None:
+        _log_decision("ACCEPT_FHT", "all constraints passed", x, weight, group_size)
+        return ValidationResult.ok()
+    param, message, reason = refusal
+    if reason is not None:
+        _log_decision("KEEP_CUDA", reason, x, weight, group_size)
+    return ValidationResult.fail(param, message)
 
 
-def _apply_act(x: torch.Tensor, act: str | None) -> torch.Tensor:
-    """The unfused input activation (comfy_kitchen's ``apply_input_act``)."""
+# ---------------------------------------------------------------- the linear
+def _unfused_act(x: torch.Tensor, act: str | None) -> torch.Tensor:
+    """comfy_kitchen's ``apply_input_act`` (the reference applies it as its own op)."""
     if act is None:
         return x
     from comfy_kitchen.backends._activations import apply_input_act
@@ -113,60 +162,25 @@ def _apply_act(x: torch.Tensor, act: str | None) -> torch.Tensor:
     return apply_input_act(x, act)
 
 
-def _kernel_accepts(x: torch.Tensor, group_size: int) -> bool:
-    from ..kernels.int8_convrot import can_use_fht
+def quantise_activations(x2d: torch.Tensor, group_size: int, act: str | None, mode: str):
+    """``(xq, xscale)`` of ``act(x2d)``: on the kernel when ``kernel_refusal`` allows
+    it (the activation fused into the quantiser when it is one of
+    ``ops.FUSED_ACTS``), else -- or when the kernel raises, which is remembered
+    for the shape -- the eager torch rotation in ``x2d``'s dtype."""
+    from ..kernels.int8_convrot import _eager_quantize, quantize_convrot_fht
+    from ..ops import FUSED_ACTS, quantize_act
 
-    return can_use_fht(x, group_size, min_k=0)
-
-
-def _can_use_fht(x: torch.Tensor, group_size: int, mode: str) -> bool:
-    if mode not in {"auto", "fht"}:
-        return False
-    if not x.is_cuda or x.dtype not in (torch.float16, torch.bfloat16):
-        return False
-    min_k = 0 if mode == "fht" else _fht_min_k(x.device.index or 0)
-    if x.shape[1] < min_k:
-        return False
-    return _kernel_accepts(x, group_size)
-
-
-def _fht_applicable(kwargs: Mapping[str, object]):
-    """Registry call rule: accept only the ConvRot calls the kernels serve."""
-    from comfy_kitchen.constraints import ValidationResult
-
-    mode = _mode()
-    x = kwargs.get("x")
-    weight = kwargs.get("weight")
-    convrot = kwargs.get("convrot", False)
-    group_size = int(kwargs.get("convrot_groupsize", 256))
-    if not convrot:
-        return ValidationResult.fail("convrot", "TileGen only handles ConvRot")
-    if mode not in {"auto", "fht"}:
-        _log_decision("KEEP_CUDA", f"mode={mode}", x, weight, group_size)
-        return ValidationResult.fail("__tilegen__", f"mode={mode}")
-    if not isinstance(x, torch.Tensor) or not x.is_cuda or x.ndim < 2:
-        return ValidationResult.fail("x", "CUDA tensor with at least 2 dims required")
-    if x.dtype not in (torch.float16, torch.bfloat16):
-        return ValidationResult.fail("x", "fp16/bf16 input required")
-    k = x.shape[-1]
-    from ..kernels.int8_convrot import NATIVE_GROUP_SIZES
-
-    if group_size not in NATIVE_GROUP_SIZES or k % 256:
-        _log_decision("KEEP_CUDA", "unsupported group/K", x, weight, group_size)
-        return ValidationResult.fail("convrot_groupsize", "requires group in {4,16,64,256} and K divisible by 256")
-    min_k = 0 if mode == "fht" else _fht_min_k(x.device.index or 0)
-    if k < min_k:
-        _log_decision("KEEP_CUDA", f"K below min_k={min_k}", x, weight, group_size)
-        return ValidationResult.fail("x", "K below TileGen threshold")
-    if not _kernel_accepts(x.reshape(-1, k)[:1], group_size):
-        _log_decision("KEEP_CUDA", "K above the kernel's maximum", x, weight, group_size)
-        return ValidationResult.fail("x", "K above the kernel's maximum")
-    shape_key = (x.numel() // k, k, x.dtype, x.device.index)
-    if shape_key in _FAILED_FHT_SHAPES:
-        _log_decision("KEEP_CUDA", "FHT previously failed", x, weight, group_size)
-        return ValidationResult.fail("x", "FHT previously failed for this shape")
-    _log_decision("ACCEPT_FHT", "all constraints passed", x, weight, group_size)
-    return ValidationResult.ok()
+    if kernel_refusal(x2d, group_size, mode, min_k=0 if mode == "fht" else None) is None:
+        try:
+            if act is None:
+                return quantize_convrot_fht(x2d, group_size)
+            if act in FUSED_ACTS:
+                return quantize_act(x2d, group_size, act)
+            return quantize_convrot_fht(_unfused_act(x2d, act), group_size)
+        except Exception:
+            _FAILED_FHT_SHAPES.add((x2d.shape[0], x2d.shape[1], x2d.dtype, x2d.device.index))
+            LOGGER.exception("FHT failed for M=%d K=%d; using eager ConvRot", x2d.shape[0], x2d.shape[1])
+    return _eager_quantize(_unfused_act(x2d, act), group_size)
 
 
 def int8_linear(
@@ -179,89 +193,62 @@ def int8_linear(
     convrot_groupsize: int = 256,
     input_act: str | None = None,
 ) -> torch.Tensor:
-    """Backend-compatible replacement for comfy_kitchen's ``int8_linear``."""
-    if x.shape[-1] != weight.shape[-1]:
-        raise ValueError(f"input and weight inner dimensions differ: {x.shape[-1]} != {weight.shape[-1]}")
+    """Backend-compatible replacement for comfy_kitchen's ``int8_linear``.
+
+    Non-ConvRot layouts, and every call in ``eager`` mode, are comfy_kitchen's
+    own eager ``int8_linear``.  ConvRot calls: ``act(x)`` rotated and quantised
+    row-wise (``quantise_activations``), then the INT8 GEMM with the
+    dequantisation fused, the output reshaped to ``x``'s leading dims.
+    """
+    k = x.shape[-1]
+    if k != weight.shape[-1]:
+        raise ValueError(f"input and weight inner dimensions differ: {k} != {weight.shape[-1]}")
     out_dtype = out_dtype or x.dtype
     mode = _mode()
     if not convrot or mode == "eager":
-        from comfy_kitchen.backends.eager.quantization import int8_linear as eager_int8_linear
+        from comfy_kitchen.backends.eager.quantization import int8_linear as kitchen_eager
 
-        return eager_int8_linear(x, weight, weight_scale, bias=bias, out_dtype=out_dtype, convrot=convrot,
-                                 convrot_groupsize=convrot_groupsize, input_act=input_act)
-    # input_act (backend.py:201-204): the activations the quantiser fuses are
-    # applied inside it on the kernel paths; any other goes through
-    # comfy_kitchen first, and every fallback applies it unfused, as the
-    # reference does.
-    from ..ops import FUSED_ACTS
-
+        return kitchen_eager(x, weight, weight_scale, bias=bias, out_dtype=out_dtype, convrot=convrot,
+                             convrot_groupsize=convrot_groupsize, input_act=input_act)
+    if k % convrot_groupsize:
+        raise ValueError(f"ConvRot group size {convrot_groupsize} does not divide K={k}")
     act = None if input_act in (None, "none") else input_act
-    if act is not None and act not in FUSED_ACTS:
-        from comfy_kitchen.backends._activations import apply_input_act
-
-        x = apply_input_act(x, act)
-        act = None
-    shape = tuple(x.shape)
-    x2d = x.reshape(-1, x.shape[-1]).contiguous()
-    weight = weight.to(device=x.device, dtype=torch.int8)
-    if convrot:
-        if x2d.shape[1] % convrot_groupsize:
-            raise ValueError(f"ConvRot group size {convrot_groupsize} does not divide K={x2d.shape[1]}")
-        key = (x2d.shape[0], x2d.shape[1], x2d.dtype, x2d.device.index)
-        if _can_use_fht(x2d, convrot_groupsize, mode) and key not in _FAILED_FHT_SHAPES:
-            try:
-                if act is None:
-                    from ..kernels.int8_convrot import quantize_convrot_fht
-
-                    xq, xscale = quantize_convrot_fht(x2d, convrot_groupsize)
-                else:
-                    from ..ops import quantize_act
-
-                    xq, xscale = quantize_act(x2d, convrot_groupsize, act)
-            except Exception:  # a shape the kernel rejects: remember it, use eager
-                _FAILED_FHT_SHAPES.add(key)
-                LOGGER.exception("FHT failed for M=%d K=%d; using eager ConvRot", x2d.shape[0], x2d.shape[1])
-                xq, xscale = _eager_quantize_convrot(_apply_act(x2d, act), convrot_groupsize)
-        else:
-            xq, xscale = _eager_quantize_convrot(_apply_act(x2d, act), convrot_groupsize)
-    else:
-        from ..quant.rowwise import quantize_rowwise
-
-        xq, xscale = quantize_rowwise(x2d, act)
-    max_temp_mb = max(16, int(os.environ.get("TILEGEN_INT8_TEMP_MB", "256")))
-    out = int8_matmul_dequant_chunked(xq, xscale, weight, weight_scale, bias, out_dtype,
-                                      max_temp_bytes=max_temp_mb * 1024 * 1024)
-    return out.reshape(*shape[:-1], weight.shape[0])
+    lead = x.shape[:-1]
+    xq, xscale = quantise_activations(x.reshape(-1, k).contiguous(), convrot_groupsize, act, mode)
+    wq = weight.to(device=x.device, dtype=torch.int8)
+    y = int8_matmul_dequant_chunked(xq, xscale, wq, weight_scale, bias, out_dtype, max_temp_bytes=_temp_bytes())
+    return y.reshape(*lead, wq.shape[0])
 
 
+# ---------------------------------------------------------------- registration
 def install() -> bool:
-    """Register the selective backend ahead of the others (False if unavailable)."""
+    """Register the selective backend ahead of the others.  False (nothing
+    registered) when the mode is ``off`` or comfy_kitchen is unavailable."""
     global _INSTALLED
+    if _INSTALLED:
+        return True
     mode = _mode()
-    if mode == "off" or _INSTALLED:
-        return _INSTALLED
+    if mode == "off":
+        return False
     try:
         from comfy_kitchen.constraints import FunctionConstraints
         from comfy_kitchen.registry import registry
 
-        device_index = torch.cuda.current_device() if torch.cuda.is_available() else 0
-        fht_min_k = 0 if mode == "fht" else _fht_min_k(device_index)
-        base = registry.get_constraints("eager", "int8_linear")
-        if base is None:
+        eager = registry.get_constraints("eager", "int8_linear")
+        if eager is None:
             raise RuntimeError("comfy_kitchen eager int8_linear constraints are unavailable")
-        constraints = FunctionConstraints(
-            params=base.params,
-            default_devices=base.default_devices,
-            min_compute_capability=base.min_compute_capability,
-            call_rules=(*getattr(base, "call_rules", ()), _fht_applicable),
-        )
-        registry.register(BACKEND_NAME, sys.modules[__name__], {"int8_linear": constraints})
-        existing = [name for name in registry._priority if name != BACKEND_NAME]
-        registry.set_priority([BACKEND_NAME, *existing])
-        _INSTALLED = True
-        LOGGER.warning("tilegen selective FHT dispatch enabled: mode=%s FHT min K=%s temp=%s MiB priority=%s",
-                       mode, fht_min_k, os.environ.get("TILEGEN_INT8_TEMP_MB", "256"), registry._priority)
-        return True
+        # The eager backend's parameter and device constraints, plus our rule.
+        ours = FunctionConstraints(params=eager.params, default_devices=eager.default_devices,
+                                   min_compute_capability=eager.min_compute_capability,
+                                   call_rules=tuple(getattr(eager, "call_rules", ())) + (_fht_applicable,))
+        registry.register(BACKEND_NAME, sys.modules[__name__], {"int8_linear": ours})
+        registry.set_priority([BACKEND_NAME] + [b for b in registry._priority if b != BACKEND_NAME])
     except Exception:
         LOGGER.exception("tilegen: could not register the ConvRot backend")
         return False
+    _INSTALLED = True
+    dev = torch.cuda.current_device() if torch.cuda.is_available() else 0
+    LOGGER.warning("tilegen selective FHT dispatch enabled: mode=%s FHT min K=%s temp=%s MiB priority=%s",
+                   mode, 0 if mode == "fht" else _fht_min_k(dev), os.environ.get("TILEGEN_INT8_TEMP_MB", "256"),
+                   registry._priority)
+    return True

@@ -4,6 +4,11 @@ Typical wiring::
 
     weight (fp16) -> QuantizeConvRotWeight -> (wq, wscale)
     activation (fp16) -> Int8ConvRotLinear(wq, wscale) -> output (fp16)
+
+Class names, ``INPUT_TYPES``, return types and categories are the ComfyUI
+workflow format of the reference's nodes.  The linear node asks the same
+decision function as the selective backend (``backend.kernel_refusal``) whether
+the rotate+quant kernel serves its input.
 """
 from __future__ import annotations
 
@@ -13,15 +18,17 @@ import os
 import torch
 
 from ..kernels.hadamard import build_hadamard
-from ..kernels.int8_convrot import _eager_quantize, can_use_fht, quantize_convrot_fht
 from ..quant.int8_ops import int8_matmul_dequant_chunked
 from ..quant.weight import quantize_convrot_weight
+from . import backend
 
 LOGGER = logging.getLogger("tilegen.nodes")
 
+_GROUP_INPUT = ("INT", {"default": 256, "min": 4, "max": 1024, "step": 4})
+
 
 class TileGenConvRotModelConfig:
-    """MODEL passthrough that sets the TILEGEN_* runtime variables from a workflow."""
+    """MODEL passthrough that writes the TILEGEN_* runtime variables from a workflow."""
 
     @classmethod
     def INPUT_TYPES(cls):
@@ -42,18 +49,30 @@ class TileGenConvRotModelConfig:
     CATEGORY = "model/optimization/tilegen"
 
     def configure(self, model, backend, fht_min_k, fht_impl, int8_temp_mb, diagnostics):
-        os.environ["TILEGEN_CONVROT_BACKEND"] = backend
-        os.environ["TILEGEN_FHT_MIN_K"] = str(max(0, int(fht_min_k)))
-        os.environ["TILEGEN_FHT_IMPL"] = fht_impl
-        os.environ["TILEGEN_INT8_TEMP_MB"] = str(max(16, int(int8_temp_mb)))
-        os.environ["TILEGEN_DIAGNOSTICS"] = "1" if diagnostics else "0"
+        settings = {
+            "TILEGEN_CONVROT_BACKEND": backend,
+            "TILEGEN_FHT_MIN_K": str(max(0, int(fht_min_k))),
+            "TILEGEN_FHT_IMPL": fht_impl,
+            "TILEGEN_INT8_TEMP_MB": str(max(16, int(int8_temp_mb))),
+            "TILEGEN_DIAGNOSTICS": "1" if diagnostics else "0",
+        }
+        os.environ.update(settings)
         LOGGER.warning("tilegen workflow config: backend=%s min_k=%s impl=%s temp=%sMiB diagnostics=%s",
                        backend, fht_min_k, fht_impl, int8_temp_mb, diagnostics)
         return (model,)
 
 
+def _resolve_device(choice: str) -> str:
+    cuda = torch.cuda.is_available()
+    if choice == "auto":
+        return "cuda" if cuda else "cpu"
+    if choice == "cuda" and not cuda:
+        raise RuntimeError("CUDA was requested but torch.cuda.is_available() is false")
+    return choice
+
+
 class ConvRotTestTensors:
-    """Deterministic (x, weight) tensors for a standalone ConvRot test graph."""
+    """Seeded (x, weight) tensors that make a standalone ConvRot test branch runnable."""
 
     @classmethod
     def INPUT_TYPES(cls):
@@ -62,7 +81,7 @@ class ConvRotTestTensors:
                 "rows": ("INT", {"default": 32, "min": 1, "max": 4096, "step": 1}),
                 "in_features": ("INT", {"default": 5120, "min": 4, "max": 32768, "step": 4}),
                 "out_features": ("INT", {"default": 256, "min": 1, "max": 32768, "step": 1}),
-                "group_size": ("INT", {"default": 256, "min": 4, "max": 1024, "step": 4}),
+                "group_size": _GROUP_INPUT,
                 "seed": ("INT", {"default": 20260726, "min": 0, "max": 0x7FFFFFFFFFFFFFFF}),
                 "dtype": (["float16", "bfloat16"], {"default": "float16"}),
                 "device": (["auto", "cuda", "cpu"], {"default": "auto"}),
@@ -75,17 +94,15 @@ class ConvRotTestTensors:
     CATEGORY = "quantization/convrot/testing"
 
     def create(self, rows, in_features, out_features, group_size, seed, dtype, device):
-        if in_features % group_size != 0:
+        if in_features % group_size:
             raise ValueError(f"in_features={in_features} must be divisible by group_size={group_size}")
-        build_hadamard(group_size, "cpu", torch.float32)  # validates the group size
-        dev = ("cuda" if torch.cuda.is_available() else "cpu") if device == "auto" else device
-        if dev == "cuda" and not torch.cuda.is_available():
-            raise RuntimeError("CUDA was requested but torch.cuda.is_available() is false")
-        dt = torch.float16 if dtype == "float16" else torch.bfloat16
-        g = torch.Generator(device=dev)
-        g.manual_seed(int(seed))
-        x = torch.randn((rows, in_features), generator=g, device=dev, dtype=dt)
-        w = torch.randn((out_features, in_features), generator=g, device=dev, dtype=dt) * 0.02
+        build_hadamard(group_size, "cpu", torch.float32)  # raises for a group that is not a power of four
+        dev = _resolve_device(device)
+        dt = {"float16": torch.float16, "bfloat16": torch.bfloat16}[dtype]
+        gen = torch.Generator(device=dev).manual_seed(int(seed))
+        # x first, then the weight, from one generator (N(0,1) and N(0, 0.02)).
+        x = torch.randn((rows, in_features), generator=gen, device=dev, dtype=dt)
+        w = torch.randn((out_features, in_features), generator=gen, device=dev, dtype=dt) * 0.02
         return (x, w)
 
 
@@ -94,8 +111,7 @@ class QuantizeConvRotWeight:
 
     @classmethod
     def INPUT_TYPES(cls):
-        return {"required": {"weight": ("TENSOR",),
-                             "group_size": ("INT", {"default": 256, "min": 4, "max": 1024, "step": 4})}}
+        return {"required": {"weight": ("TENSOR",), "group_size": _GROUP_INPUT}}
 
     RETURN_TYPES = ("TENSOR", "TENSOR")
     RETURN_NAMES = ("weight_quantized", "weight_scale")
@@ -107,7 +123,12 @@ class QuantizeConvRotWeight:
 
 
 class Int8ConvRotLinear:
-    """INT8 ConvRot linear: fused rotate+quant -> fused INT8 GEMM + dequant."""
+    """INT8 ConvRot linear: rotate+quant of the activations, then the INT8 GEMM + dequant.
+
+    The mode is TILEGEN_CONVROT_BACKEND when set, else the node's ``backend``
+    input.  The node's ``auto`` threshold is TILEGEN_FHT_MIN_K, else 8192 (5120
+    on sm_75) on pre-Blackwell GPUs and 0 on Blackwell, as the backend's.
+    """
 
     @classmethod
     def INPUT_TYPES(cls):
@@ -116,7 +137,7 @@ class Int8ConvRotLinear:
                 "x": ("TENSOR",),
                 "weight_quantized": ("TENSOR",),
                 "weight_scale": ("TENSOR",),
-                "group_size": ("INT", {"default": 256, "min": 4, "max": 1024, "step": 4}),
+                "group_size": _GROUP_INPUT,
             },
             "optional": {"bias": ("TENSOR",), "backend": (["auto", "fht", "eager"], {"default": "auto"})},
         }
@@ -127,31 +148,17 @@ class Int8ConvRotLinear:
     CATEGORY = "quantization/convrot"
 
     def forward(self, x, weight_quantized, weight_scale, group_size, bias=None, backend="auto"):
-        shape = tuple(x.shape)
-        x2d = x.reshape(-1, x.shape[-1]).contiguous()
-        k = x2d.shape[1]
-        n = weight_quantized.shape[0]
-        if k % group_size != 0:
+        k = x.shape[-1]
+        if k % group_size:
             raise ValueError(f"K={k} must be divisible by group_size={group_size}")
-        # The environment variable overrides the node input (nodes.py:180).
         mode = os.environ.get("TILEGEN_CONVROT_BACKEND", backend).strip().lower()
-        if mode in {"auto", "fht"} and self._can_use_fht(x2d, group_size, mode):
-            try:
-                xq, xscale = quantize_convrot_fht(x2d, group_size)
-            except Exception as e:  # pragma: no cover
-                print(f"[Int8ConvRotLinear] FHT failed, using eager: {e}")
-                xq, xscale = _eager_quantize(x2d, group_size)
-        else:
-            xq, xscale = _eager_quantize(x2d, group_size)
+        xq, xscale = _node_quantise(x.reshape(-1, k).contiguous(), group_size, mode)
         wq = weight_quantized.to(device=x.device, dtype=torch.int8)
-        out = int8_matmul_dequant_chunked(xq, xscale, wq, weight_scale, bias, x.dtype)
-        return (out.reshape(*shape[:-1], n),)
+        y = int8_matmul_dequant_chunked(xq, xscale, wq, weight_scale, bias, x.dtype)
+        return (y.reshape(*x.shape[:-1], wq.shape[0]),)
 
-    @staticmethod
-    def _can_use_fht(x: torch.Tensor, group_size: int, mode: str) -> bool:
-        min_k = 0
-        if mode == "auto":
-            from .backend import _fht_min_k
 
-            min_k = _fht_min_k(x.device.index or 0) if x.is_cuda else 0
-        return can_use_fht(x, group_size, min_k=min_k)
+def _node_quantise(x2d: torch.Tensor, group_size: int, mode: str):
+    # "eager" (or anything but auto/fht) makes kernel_refusal decline, so the
+    # eager rotation runs, as in the reference node.
+    return backend.quantise_activations(x2d, group_size, None, mode if mode in ("auto", "fht") else "eager")

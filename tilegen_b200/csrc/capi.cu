@@ -816,10 +816,15 @@ int tg_int8_gemm_dequant_splitk_noalloc(const int8_t* xq, const float* xscale, c
   if (!current_device(&dev, &info)) return TG_ERR_CUDA;
   uint8_t* scratch = nullptr;
   if (!noalloc_scratch(dev, &scratch)) return TG_ERR_CUDA;
-  // Every call shares the array: zero the counters and this call's part of the
-  // accumulator first, in stream order (a memset, not an allocation).
+  // Every call shares the array: when the sums go through it (K split more
+  // than a cluster holds), zero the counters and this call's part of the
+  // accumulator first, in stream order (a memset, not an allocation).  The
+  // cluster form sums in shared memory and never touches the array.
+  int slices = 0, cluster = 0;
+  const int cfg = tg_int8_gemm_dequant_splitk_config(M, N, K, out_dtype, bias != nullptr, &slices, &cluster);
+  if (cfg != TG_OK) return cfg;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(scratch, 0, kNoAllocCountBytes + size_t(M) * size_t(N) * 4, st) != cudaSuccess)
+  if (!cluster && cudaMemsetAsync(scratch, 0, kNoAllocCountBytes + size_t(M) * size_t(N) * 4, st) != cudaSuccess)
     return TG_ERR_CUDA;
   return splitk_launch(xq, xscale, wq, wscale, wscale_numel, bias, bias_dtype, M, N, K, out_dtype, out,
                        reinterpret_cast<uint32_t*>(scratch), reinterpret_cast<int32_t*>(scratch + kNoAllocCountBytes),

@@ -18,7 +18,8 @@
 //   warps 2-5   epilogue: tcgen05.ld 32 rows x one chunk of columns, int32 ->
 //               fp32 (round to nearest), * xscale, * wscale, + bias, convert,
 //               then a swizzled shared-memory chunk stored by a TMA bulk tensor
-//               store.
+//               store (two staging chunks per warp where shared memory allows,
+//               so a chunk's conversion overlaps the previous chunk's store).
 // PAIR = false: each CTA computes a 128 x BN tile (cta_group::1, M=128).
 // PAIR = true: the two CTAs of a cluster compute one 256 x BN tile with the
 //   pair MMA (cta_group::2, M=256): each CTA loads its 128 rows of A and half
@@ -56,13 +57,20 @@ __host__ __device__ constexpr int ksub(bool pair) { return pair ? 2 : 1; }
 __host__ __device__ constexpr uint32_t stage_bytes(int bn, bool pair) {
   return uint32_t(ksub(pair) * (A_BYTES + b_rows(bn, pair) * BK));
 }
-__host__ __device__ constexpr int stages(int bn, bool pair) {
-  return int((SMEM_LIMIT - 4 * OUT_BYTES - 1024 - 4096) / stage_bytes(bn, pair)) > 8
+__host__ __device__ constexpr int stages_with(int bn, bool pair, int nbuf) {
+  return int((SMEM_LIMIT - 4 * nbuf * OUT_BYTES - 1024 - 4096) / stage_bytes(bn, pair)) > 8
              ? 8
-             : int((SMEM_LIMIT - 4 * OUT_BYTES - 1024 - 4096) / stage_bytes(bn, pair));
+             : int((SMEM_LIMIT - 4 * nbuf * OUT_BYTES - 1024 - 4096) / stage_bytes(bn, pair));
 }
+// Staging chunks per epilogue warp: two (one is converted while the TMA store
+// of the other reads it) when the second costs the operand ring no slot, else
+// one.  Two for the 160- to 224-wide pair tiles, one for 256 and 128.
+__host__ __device__ constexpr int out_bufs(int bn, bool pair) {
+  return stages_with(bn, pair, 2) >= stages_with(bn, pair, 1) ? 2 : 1;
+}
+__host__ __device__ constexpr int stages(int bn, bool pair) { return stages_with(bn, pair, out_bufs(bn, pair)); }
 __host__ __device__ constexpr uint32_t smem_bytes(int bn, bool pair) {
-  return uint32_t(stages(bn, pair)) * stage_bytes(bn, pair) + 4 * OUT_BYTES + 1024;
+  return uint32_t(stages(bn, pair)) * stage_bytes(bn, pair) + uint32_t(4 * out_bufs(bn, pair)) * OUT_BYTES + 1024;
 }
 
 // tcgen05 instruction descriptor: D=S32 (bits 4-5 = 2), A=B=S8 (bits 7-9 and
@@ -125,6 +133,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   constexpr int CH = CH_BYTES / ESZ;   // output columns per epilogue chunk
   constexpr int NCH = BN / CH;         // chunks per tile
   constexpr int S = stages(BN, PAIR);
+  constexpr int NBUF = out_bufs(BN, PAIR);
   constexpr int BROWS = b_rows(BN, PAIR);
   constexpr int KS = ksub(PAIR);
   constexpr uint32_t B_BYTES = uint32_t(BROWS) * BK;       // one 128-byte K sub-block of B
@@ -287,7 +296,8 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int et = threadIdx.x - 64;      // 0..127
     const int quarter = warp & 3;         // TMEM lanes [32*quarter, +32)
-    uint8_t* sbuf = sOut + (warp - 2) * OUT_BYTES;
+    uint8_t* const sbufs = sOut + (warp - 2) * NBUF * OUT_BYTES;
+    int chunk_seq = 0;  // chunks this warp has staged; every chunk commits one bulk group
     const uint32_t tempty_leader0 = PAIR ? mapa_shared(smem_u32(&tempty_bar[0]), 0) : 0u;
     const uint32_t tempty_leader1 = PAIR ? mapa_shared(smem_u32(&tempty_bar[1]), 0) : 0u;
     int local = 0;
@@ -338,8 +348,11 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
             else mbar_arrive(&tempty_bar[ab]);
           }
         }
-        // The previous chunk's TMA store must have finished reading sbuf.
-        if (lane == 0) bulk_wait_read<0>();
+        // The TMA store that last used this staging chunk (NBUF chunks ago)
+        // must have finished reading it; later stores may still be in flight.
+        uint8_t* const sbuf = sbufs + (chunk_seq % NBUF) * OUT_BYTES;
+        ++chunk_seq;
+        if (lane == 0) bulk_wait_read<NBUF - 1>();
         __syncwarp();
 
         const float* cws = col_ws + ch * CH;
@@ -388,9 +401,12 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        // A box that starts past the last row/column would store nothing; skip it.
-        if (lane == 0 && m0 + quarter * 32 < p.M && n0 + ch * CH < p.N) {
-          tma_store_2d(&tma_out, sbuf, n0 + ch * CH, m0 + quarter * 32);
+        // A box that starts past the last row/column would store nothing; skip
+        // it, but still commit a (then empty) group so that the count of
+        // groups behind each staging chunk stays one per chunk.
+        if (lane == 0) {
+          if (m0 + quarter * 32 < p.M && n0 + ch * CH < p.N)
+            tma_store_2d(&tma_out, sbuf, n0 + ch * CH, m0 + quarter * 32);
           bulk_commit();
         }
       }

@@ -12,8 +12,7 @@
  * Device-side failures (a bounded wait that gave up) are recorded in a device
  * status word that tg_device_status() reads.
  *
- * The Python package binds these with ctypes (tilegen_b200/_lib.py); the
- * reference-side binding a maintainer would add is shown in INTEGRATION.md.
+ * The Python package binds these with ctypes (tilegen_b200/_lib.py).
  */
 #ifndef TILEGEN_B200_H
 #define TILEGEN_B200_H

@@ -64,3 +64,34 @@ def test_host_linear_graph_replays(cuda, m, k, n, chunk):
         ref = ops.int8_gemm_dequant(*ops.rotate_quant(x.to(cuda), 256), wq, ws, bias, torch.bfloat16).cpu()
         assert r is out
         assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), f"call {i}"
+
+
+def test_two_host_linear_graphs_replayed_concurrently(cuda):
+    """Two captured graphs whose chunks run the split-K kernel, replayed at the same
+    time on two streams: each graph owns its split-K scratch, so both stay exact."""
+    from tilegen_b200 import streaming
+
+    m, k, n, chunk = 600, 13824, 640, 128
+    w = gaussian_weight(n, k, seed=7, dtype=torch.bfloat16, device=cuda)
+    wq, ws = ops.rotate_quant(w, 256)
+    xs = [outlier_activations(m, k, seed=20 + j, dtype=torch.bfloat16) for j in range(2)]
+    hosts = [x.pin_memory() for x in xs]
+    outs = [torch.empty((m, n), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    refs = [ops.int8_gemm_dequant(*ops.rotate_quant(x.to(cuda), 256), wq, ws, None, torch.bfloat16).cpu() for x in xs]
+    streams = [torch.cuda.Stream(device=cuda) for _ in range(2)]
+    for j in range(2):  # capture both graphs
+        with torch.cuda.stream(streams[j]):
+            int8_linear_host(hosts[j], wq, ws, None, torch.bfloat16, out=outs[j], rows_per_chunk=chunk, graph=True)
+        streams[j].synchronize()
+    held = [e[1] for e in list(streaming._GRAPHS.values())[-2:]]  # the two graphs just captured
+    scratch_ptrs = {t.data_ptr() for h in held for t in h if t.dtype == torch.uint8}
+    assert len(scratch_ptrs) == 2  # one split-K scratch per graph
+    for _ in range(3):
+        for o in outs:
+            o.zero_()
+        for j in range(2):
+            with torch.cuda.stream(streams[j]):
+                int8_linear_host(hosts[j], wq, ws, None, torch.bfloat16, out=outs[j], rows_per_chunk=chunk, graph=True)
+        torch.cuda.synchronize()
+        for j in range(2):
+            assert torch.equal(outs[j].view(torch.int16), refs[j].view(torch.int16)), j

@@ -102,7 +102,9 @@ def int8_linear_host(x_host: torch.Tensor, weight: torch.Tensor, weight_scale: t
     first call with a given set of buffers (x_host, out, weight, scales, bias:
     addresses, shapes and dtypes) runs eagerly and captures the graph, later calls
     with the same buffers replay it (it reads whatever they hold then).  Up to four
-    graphs are kept, each holding its device buffers.
+    graphs are kept, each holding its device buffers (its split-K scratch
+    included, so different graphs may be replayed concurrently; one graph's
+    replays must not overlap each other, like any CUDA graph's).
     """
     if x_host.is_cuda:
         raise ValueError("int8_linear_host: x_host must be in host memory (use int8_linear for CUDA tensors)")
@@ -147,8 +149,14 @@ def int8_linear_host(x_host: torch.Tensor, weight: torch.Tensor, weight_scale: t
         # First call: run it eagerly on the capture stream (one-time launch
         # set-up, and any split-K scratch, which is cached per stream, is made
         # and zeroed outside the capture), then capture the same sequence there.
+        # The graph gets a split-K scratch of its own: the capture stream's
+        # cached one is dropped from the cache before the eager run and the new
+        # one taken out of it after the capture, so graphs replayed at the same
+        # time on different streams never share a scratch.
         cur = torch.cuda.current_stream(idx)
         cap = _streams(idx)[2]
+        ws_key = (idx, cap.cuda_stream)
+        ops._SPLITK_WS.pop(ws_key, None)
         cap.wait_stream(cur)
         with torch.cuda.stream(cap):
             _enqueue(*args)
@@ -157,9 +165,9 @@ def int8_linear_host(x_host: torch.Tensor, weight: torch.Tensor, weight_scale: t
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=cap):
             held = _enqueue(*args)
-        scratch = ops._SPLITK_WS.get((idx, cap.cuda_stream))
+        scratch = ops._SPLITK_WS.pop(ws_key, None)
         if scratch is not None:
-            held.append(scratch)  # the graph's kernels use this very buffer
+            held.append(scratch)  # the graph's kernels use this very buffer, and only this graph
         with _GRAPH_LOCK:
             _GRAPHS[key] = (g, held)
             while len(_GRAPHS) > _GRAPH_CACHE_SIZE:

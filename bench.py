@@ -50,11 +50,14 @@ NOMINAL_INT8_TOPS = 4500.0
 PUBLISHED_QKV_US = 10550.0  # RTX 2080 Ti, tilegen FHT int8_convrot qkv_proj, README.md:9
 METRIC = "int8_convrot linear us (M=4096) & speedup vs bf16 cuBLAS; quantizer HBM GB/s"
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each
-# kernel on this workload, from an ncu capture on a B200.  The quantiser's 21 MB
-# of codes are still in L2 when it ends, so its traffic is below its algorithmic
-# bytes; the GEMM's equals A + B + the part of the output already written back.
-GEMM_TRAFFIC_BYTES = 100_555_776 + 93_888_512
-QUANT_TRAFFIC_BYTES = 41_979_392 + 571_392
+# kernel in this bench's timed loop, from one ncu capture of the current kernels
+# on a B200 (the files named below).  The quantiser's 21 MB of codes are still in
+# L2 when it ends, so its traffic is below its algorithmic bytes; the GEMM's
+# equals A + B + the part of the output already written back.
+GEMM_TRAFFIC_BYTES = 100_430_592 + 95_247_872
+QUANT_TRAFFIC_BYTES = 41_977_344 + 174_592
+GEMM_TRAFFIC_SOURCE = "profiles/gemm_i8_dequant_pair_qkv.md"
+QUANT_TRAFFIC_SOURCE = "profiles/rotquant_short_m4096_k5120.md"
 
 
 def _peaks():
@@ -749,13 +752,14 @@ def run_tilegen(args):
         "roofline": {"bound": "tensor", "kernel": "gemm_i8_dequant_kernel", "achieved": round(gemm_tops, 1),
                      "peak": round(int8_peak, 1), "unit": "TOP/s", "frac": round(gemm_tops / int8_peak, 4),
                      "peak_source": f"2 x {peak_kind} bf16 cuBLAS burst (dense int8 = 2 x dense bf16)",
-                     "traffic": GEMM_TRAFFIC_BYTES, "algorithmic_ops_per_launch": 2 * m * n * k,
+                     "traffic": GEMM_TRAFFIC_BYTES, "traffic_source": GEMM_TRAFFIC_SOURCE,
+                     "algorithmic_ops_per_launch": 2 * m * n * k,
                      "vs_cublaslt_int8_tops": round(int8_lib_tops, 1),
                      "vs_nominal_int8": round(gemm_tops / NOMINAL_INT8_TOPS, 4)},
         "quant_roofline": {"bound": "hbm", "kernel": "rotquant_kernel", "achieved": round(quant_gbs, 1),
                            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(quant_gbs / peaks["hbm_gbs"], 4),
                            "peak_source": peak_kind, "algorithmic_bytes_per_launch": quant_bytes,
-                           "traffic": QUANT_TRAFFIC_BYTES},
+                           "traffic": QUANT_TRAFFIC_BYTES, "traffic_source": QUANT_TRAFFIC_SOURCE},
         "e2e": {"value": round(e2e_plugin_us, 2), "unit": "us", "h2d_bytes_per_step": x.numel() * 2,
                 "d2h_bytes_per_step": m * n * 2,
                 "path": "one stream: pinned host x -> device, tilegen.comfyui.backend.int8_linear(convrot=True) "

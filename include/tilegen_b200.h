@@ -207,6 +207,29 @@ int tg_set_gemm_config(int bn, int pair);
  */
 int tg_device_status(int device, uint32_t *bits, int clear);
 
+/*
+ * Peer memory for the optional output all-gather of a row-sharded linear (one
+ * process per GPU on one node).  No reference counterpart: the reference runs
+ * on one GPU.
+ *
+ * tg_peer_alloc: `bytes` of device memory on the current device (cudaMalloc)
+ *   and its interprocess handle, tg_peer_handle_bytes() bytes written to
+ *   `handle`; free with tg_peer_free.
+ * tg_peer_open: map another process's buffer from its handle into the current
+ *   device's address space (peer access enabled on demand); *ptr is usable as
+ *   a device pointer in copies.  A process cannot open its own handles.  Unmap
+ *   with tg_peer_close.
+ * tg_copy_async: enqueue a copy of `bytes` between device pointers (local or
+ *   mapped peer memory) on `stream`; between GPUs it runs on a copy engine over
+ *   NVLink and uses no SMs.
+ */
+size_t tg_peer_handle_bytes(void);
+int tg_peer_alloc(size_t bytes, void **ptr, void *handle);
+int tg_peer_free(void *ptr);
+int tg_peer_open(const void *handle, void **ptr);
+int tg_peer_close(void *ptr);
+int tg_copy_async(void *dst, const void *src, size_t bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

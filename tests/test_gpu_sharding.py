@@ -65,3 +65,67 @@ def test_sharded_linear_equals_single_gpu_nccl(m):
             pytest.fail("a rank hung")
     res = sorted(q.get(timeout=10) for _ in procs)
     assert all(r[1] for r in res), res
+
+
+def _peer_worker(rank, world, port, m, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from tilegen_b200 import ops
+    from tilegen_b200.kernels.int8_convrot import quantize_convrot
+    from tilegen_b200.quant import int8_matmul_dequant_chunked, quantize_convrot_weight
+    from tilegen_b200.sharding import PeerRowGather, local_rows
+    from tilegen_b200.synthetic import gaussian_weight, outlier_activations
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    g = None
+    try:
+        wq, ws = quantize_convrot_weight(gaussian_weight(1024, 5120, seed=1, dtype=torch.bfloat16).to(dev), 256)
+        g = PeerRowGather(m, 1024, torch.bfloat16, dev)
+        other = torch.randn(4096, 4096, device=dev)
+        ok = True
+        for step in range(4):  # both buffers, each used twice
+            x = outlier_activations(m, 5120, seed=10 + step, dtype=torch.bfloat16).to(dev)
+            xq, xs = quantize_convrot(local_rows(x, world, rank), 256, backend="fht")
+            ops.int8_gemm_dequant(xq, xs, wq, ws, None, torch.bfloat16, out=g.local())
+            pending = g.start()
+            other = other @ other.t() * 1e-4  # kernels in flight while the copy engines run
+            y = pending.wait()
+            xq, xs = quantize_convrot(x, 256, backend="fht")
+            ref = int8_matmul_dequant_chunked(xq, xs, wq, ws, None, torch.bfloat16)
+            ok = ok and bool(torch.equal(y, ref)) and tuple(y.shape) == (m, 1024)
+        q.put((rank, ok, m))
+    except Exception as e:  # report, never hang
+        q.put((rank, False, f"{type(e).__name__}: {e}"[:300]))
+    finally:
+        if g is not None:
+            g.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("m", [4096, 8191])
+def test_peer_copy_gather_equals_single_gpu(m):
+    """PeerRowGather (copy engines over NVLink, no SMs): four steps alternating its two
+    buffers, each step's rows written by the GEMM straight into the mapped buffer, a
+    matmul in flight during the copies; every step equals the single-GPU output."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, m, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung")
+    res = sorted(q.get(timeout=10) for _ in procs)
+    assert all(r[1] for r in res), res

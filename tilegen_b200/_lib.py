@@ -119,6 +119,17 @@ def lib() -> ctypes.CDLL:
         L.tg_int8_gemm_dequant_splitk_config.argtypes = [i64, i64, i64, i32, i32, ctypes.POINTER(i32),
                                                          ctypes.POINTER(i32)]
         L.tg_int8_gemm_dequant_splitk_config.restype = i32
+        L.tg_peer_handle_bytes.restype = ctypes.c_size_t
+        L.tg_peer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(p), p]
+        L.tg_peer_alloc.restype = i32
+        L.tg_peer_free.argtypes = [p]
+        L.tg_peer_free.restype = i32
+        L.tg_peer_open.argtypes = [p, ctypes.POINTER(p)]
+        L.tg_peer_open.restype = i32
+        L.tg_peer_close.argtypes = [p]
+        L.tg_peer_close.restype = i32
+        L.tg_copy_async.argtypes = [p, p, ctypes.c_size_t, p]
+        L.tg_copy_async.restype = i32
         _lib = L
     return _lib
 

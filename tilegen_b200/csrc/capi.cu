@@ -832,3 +832,56 @@ int tg_int8_gemm_dequant_splitk_noalloc(const int8_t* xq, const float* xscale, c
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ peer memory
+// Buffers that other processes on this node (one per GPU) can map, and copies
+// between mapped buffers on a stream.  cudaMemcpyAsync between this device and
+// a peer's mapped memory runs on a copy engine over NVLink, using no SMs.
+extern "C" {
+
+size_t tg_peer_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int tg_peer_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return TG_ERR_INVALID_ARG;
+  *ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return TG_ERR_CUDA;
+  if (cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p) != cudaSuccess) {
+    cudaFree(p);
+    return TG_ERR_CUDA;
+  }
+  *ptr = p;
+  return TG_OK;
+}
+
+int tg_peer_free(void* ptr) {
+  if (!ptr) return TG_ERR_INVALID_ARG;
+  return cudaFree(ptr) == cudaSuccess ? TG_OK : TG_ERR_CUDA;
+}
+
+int tg_peer_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return TG_ERR_INVALID_ARG;
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return TG_ERR_CUDA;
+  *ptr = p;
+  return TG_OK;
+}
+
+int tg_peer_close(void* ptr) {
+  if (!ptr) return TG_ERR_INVALID_ARG;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? TG_OK : TG_ERR_CUDA;
+}
+
+int tg_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return TG_OK;
+  if (!dst || !src) return TG_ERR_INVALID_ARG;
+  return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? TG_OK
+             : TG_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -132,11 +132,13 @@ def quantize_act(x: torch.Tensor, group: int = 256, act: str | None = None, orde
 
 
 def int8_gemm_dequant(xq: torch.Tensor, xscale: torch.Tensor, wq: torch.Tensor, wscale: torch.Tensor,
-                      bias: torch.Tensor | None, out_dtype: torch.dtype) -> torch.Tensor:
+                      bias: torch.Tensor | None, out_dtype: torch.dtype, out: torch.Tensor | None = None) -> torch.Tensor:
     """``((float(xq @ wq.T) * xscale[:, None]) * wscale[None, :]) + bias`` as ``out_dtype``.
 
     ``xq [M, K]`` and ``wq [N, K]`` int8 on the same CUDA device; ``xscale [M]``;
-    ``wscale`` scalar or ``[N]``; ``bias [N]`` fp32/fp16/bf16 or None.
+    ``wscale`` scalar or ``[N]``; ``bias [N]`` fp32/fp16/bf16 or None.  ``out``: an
+    optional contiguous ``[M, N]`` ``out_dtype`` tensor on that device (16-byte
+    aligned) to write into, e.g. this rank's rows of a ``PeerRowGather`` buffer.
     """
     if not (xq.is_cuda and wq.is_cuda):
         raise ValueError("int8_gemm_dequant: CUDA tensors required")
@@ -167,7 +169,12 @@ def int8_gemm_dequant(xq: torch.Tensor, xscale: torch.Tensor, wq: torch.Tensor, 
             raise ValueError(f"int8_gemm_dequant: bias has {b.numel()} elements, expected {n}")
         bias = b
         b_ptr, b_code = b.data_ptr(), _DTYPE_CODE[b.dtype]
-    out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    elif (tuple(out.shape) != (m, n) or out.dtype != out_dtype or out.device != dev or not out.is_contiguous()
+          or out.data_ptr() % 16):
+        raise ValueError(f"int8_gemm_dequant: out must be a contiguous 16-byte aligned [{m}, {n}] {out_dtype} "
+                         f"tensor on {dev}")
     if m and splitk_route(m, n, k):
         work = _splitk_workspace(dev, m, n)
         _call("tg_int8_gemm_dequant_splitk", dev, xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),

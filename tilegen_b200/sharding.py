@@ -12,8 +12,15 @@ where the gathered output is used.
 Blocks are ``ceil(M / world)`` rows; the last rank's block may be short or
 empty.  ``gather_rows`` pads the short blocks to the common size for the
 collective and trims the result.
+
+``PeerRowGather`` is the same gather for a caller that repeats it every step:
+each rank writes its rows straight into a buffer that every peer has mapped,
+and the peers' blocks are pulled in by the GPU's copy engines over NVLink, so
+the transfer uses no SMs and the next layer's kernels keep all of them.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -78,6 +85,145 @@ def gather_rows(y_local: torch.Tensor, m_total: int, group=None, async_op: bool 
         out = None if async_op else torch.cat(parts, 0)
     handle = RowGather(work if async_op else None, out, parts if async_op else None, m_total)
     return handle if async_op else handle.wait()
+
+
+class _DeviceArray:
+    """A raw device buffer seen by torch through ``__cuda_array_interface__`` (no copy)."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+_INT_VIEW = {1: (torch.int8, "|i1"), 2: (torch.int16, "<i2"), 4: (torch.int32, "<i4")}
+
+
+class PeerGather:
+    """A ``PeerRowGather.start()`` in flight; ``wait()`` orders the caller's current
+    stream after the copies and returns the gathered ``[m_total, N]`` tensor."""
+
+    def __init__(self, events: list, out: torch.Tensor):
+        self._events, self._out = events, out
+
+    def wait(self) -> torch.Tensor:
+        cur = torch.cuda.current_stream(self._out.device)
+        for ev in self._events:
+            cur.wait_event(ev)
+        self._events = []
+        return self._out
+
+
+class PeerRowGather:
+    """Row all-gather by copy engines over NVLink, for one process per GPU on one node.
+
+    Set up once per output shape (``m_total`` rows of ``n`` columns of ``dtype``):
+    every rank allocates two buffers of the full ``[world * ceil(m_total / world), n]``
+    output and maps its peers' (interprocess handles, exchanged once).  Each step:
+
+    1. write this rank's rows into ``local()`` (e.g. as the GEMM's output);
+    2. ``start()``: once every rank has reached its own ``start()`` in stream order
+       (a one-element NCCL all-reduce, on a side stream), one copy per peer pulls
+       that peer's block from its buffer into this rank's, on separate streams, so
+       several copy engines run at once; nothing waits on the host;
+    3. ``wait()`` on the returned handle (the caller's current stream waits for the
+       copies) gives the full output.  Kernels enqueued between ``start()`` and
+       ``wait()`` overlap the transfer and keep every SM.
+
+    The two buffers alternate between steps, so a step's rows may be written while
+    peers may still copy the previous step's.  Call ``wait()`` on one step's gather
+    before writing the rows of the step after the next one (in practice: wait on
+    each step before starting the next).  Every rank calls ``start()`` the same
+    number of times, in the same order as its other collectives.  ``close()`` frees
+    the buffers (a barrier, so no peer still reads them); tensors returned earlier
+    must not be used after it.
+    """
+
+    def __init__(self, m_total: int, n: int, dtype: torch.dtype, device=None, group=None):
+        from . import _lib
+
+        self._L = _lib.lib()
+        self._check = _lib.check
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.m, self.n, self.dtype = int(m_total), int(n), dtype
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.per = -(-self.m // self.world)
+        esize = torch.empty(0, dtype=dtype).element_size()
+        self.row_bytes = self.n * esize
+        self.bounds = [shard_bounds(self.m, self.world, r) for r in range(self.world)]
+        total = max(1, self.world * self.per * self.row_bytes)
+        hb = int(self._L.tg_peer_handle_bytes())
+        int_dt, typestr = _INT_VIEW[esize]
+        self._own, self._views, handles = [], [], []
+        with torch.cuda.device(self.device):
+            for _ in range(2):
+                ptr, h = ctypes.c_void_p(), ctypes.create_string_buffer(hb)
+                self._check("tg_peer_alloc", self._L.tg_peer_alloc(total, ctypes.byref(ptr), h))
+                self._own.append(ptr.value)
+                handles.append(h.raw)
+                arr = _DeviceArray(ptr.value, (self.world * self.per, self.n), typestr)
+                self._views.append(torch.as_tensor(arr, device=self.device).view(int_dt).view(dtype))
+            gathered = [None] * self.world
+            dist.all_gather_object(gathered, handles, group=group)
+            self._peer = [[None] * self.world for _ in range(2)]
+            for r in range(self.world):
+                if r == self.rank:
+                    continue
+                for b in range(2):
+                    ptr = ctypes.c_void_p()
+                    self._check("tg_peer_open", self._L.tg_peer_open(gathered[r][b], ctypes.byref(ptr)))
+                    self._peer[b][r] = ptr.value
+            self._copy_streams = [torch.cuda.Stream(self.device) for _ in range(max(1, self.world - 1))]
+            self._sync_stream = torch.cuda.Stream(self.device)
+            self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self._buf = 0
+        self._closed = False
+
+    def local(self) -> torch.Tensor:
+        """This rank's rows of the buffer the next ``start()`` gathers (write them first)."""
+        s, e = self.bounds[self.rank]
+        return self._views[self._buf][s:e]
+
+    def start(self) -> PeerGather:
+        b = self._buf
+        cur = torch.cuda.current_stream(self.device)
+        ready = torch.cuda.Event()
+        ready.record(cur)
+        self._sync_stream.wait_event(ready)
+        with torch.cuda.stream(self._sync_stream):
+            dist.all_reduce(self._flag, group=self.group, async_op=True).wait()
+        events, j = [], 0
+        for r in range(self.world):
+            s, e = self.bounds[r]
+            if r == self.rank or e <= s:
+                continue
+            st = self._copy_streams[j]
+            j += 1
+            st.wait_stream(self._sync_stream)
+            off = s * self.row_bytes
+            self._check("tg_copy_async", self._L.tg_copy_async(self._own[b] + off, self._peer[b][r] + off,
+                                                               (e - s) * self.row_bytes, st.cuda_stream))
+            ev = torch.cuda.Event()
+            ev.record(st)
+            events.append(ev)
+        self._buf ^= 1
+        return PeerGather(events, self._views[b][: self.m])
+
+    def close(self) -> None:
+        if self._closed:
+            return
+        self._closed = True
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every peer has finished its copies from our buffers
+        for b in range(2):
+            for r, ptr in enumerate(self._peer[b]):
+                if ptr is not None:
+                    self._L.tg_peer_close(ptr)
+        dist.barrier(group=self.group)
+        for ptr in self._own:
+            self._L.tg_peer_free(ptr)
+        self._views = []
 
 
 def int8_convrot_linear_local(x_local: torch.Tensor, wq: torch.Tensor, wscale: torch.Tensor,

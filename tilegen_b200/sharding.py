@@ -156,29 +156,61 @@ class PeerRowGather:
         hb = int(self._L.tg_peer_handle_bytes())
         int_dt, typestr = _INT_VIEW[esize]
         self._own, self._views, handles = [], [], []
+        self._peer = [[None] * self.world for _ in range(2)]
+        self._closed = True
+        # Every rank takes the same collective steps whatever fails locally, and all
+        # raise together if any rank failed, so no rank waits in a collective that a
+        # failed peer never joins.
         with torch.cuda.device(self.device):
-            for _ in range(2):
-                ptr, h = ctypes.c_void_p(), ctypes.create_string_buffer(hb)
-                self._check("tg_peer_alloc", self._L.tg_peer_alloc(total, ctypes.byref(ptr), h))
-                self._own.append(ptr.value)
-                handles.append(h.raw)
-                arr = _DeviceArray(ptr.value, (self.world * self.per, self.n), typestr)
-                self._views.append(torch.as_tensor(arr, device=self.device).view(int_dt).view(dtype))
+            self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+            err = None
+            try:
+                for _ in range(2):
+                    ptr, h = ctypes.c_void_p(), ctypes.create_string_buffer(hb)
+                    self._check("tg_peer_alloc", self._L.tg_peer_alloc(total, ctypes.byref(ptr), h))
+                    self._own.append(ptr.value)
+                    handles.append(h.raw)
+                    arr = _DeviceArray(ptr.value, (self.world * self.per, self.n), typestr)
+                    self._views.append(torch.as_tensor(arr, device=self.device).view(int_dt).view(dtype))
+            except Exception as e:  # reported below, on every rank
+                err = e
+            self._agree(err, "allocating the gather buffers")
             gathered = [None] * self.world
             dist.all_gather_object(gathered, handles, group=group)
-            self._peer = [[None] * self.world for _ in range(2)]
-            for r in range(self.world):
-                if r == self.rank:
-                    continue
-                for b in range(2):
-                    ptr = ctypes.c_void_p()
-                    self._check("tg_peer_open", self._L.tg_peer_open(gathered[r][b], ctypes.byref(ptr)))
-                    self._peer[b][r] = ptr.value
+            try:
+                for r in range(self.world):
+                    if r == self.rank:
+                        continue
+                    for b in range(2):
+                        ptr = ctypes.c_void_p()
+                        self._check("tg_peer_open", self._L.tg_peer_open(gathered[r][b], ctypes.byref(ptr)))
+                        self._peer[b][r] = ptr.value
+            except Exception as e:
+                err = e
+            self._agree(err, "mapping the peers' buffers")
             self._copy_streams = [torch.cuda.Stream(self.device) for _ in range(max(1, self.world - 1))]
             self._sync_stream = torch.cuda.Stream(self.device)
-            self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
         self._buf = 0
         self._closed = False
+
+    def _agree(self, err, what: str) -> None:
+        """All ranks learn whether any failed at ``what``; on failure each releases what
+        it holds and raises."""
+        ok = torch.tensor([0.0 if err is not None else 1.0], device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        if ok.item() == 1.0:
+            return
+        for b in range(2):
+            for r, ptr in enumerate(self._peer[b]):
+                if ptr is not None:
+                    self._L.tg_peer_close(ptr)
+                    self._peer[b][r] = None
+        torch.cuda.synchronize(self.device)
+        for ptr in self._own:
+            self._L.tg_peer_free(ptr)
+        self._own, self._views = [], []
+        raise RuntimeError(f"PeerRowGather: {what} failed on "
+                           f"{'this rank' if err is not None else 'another rank'}: {err}")
 
     def local(self) -> torch.Tensor:
         """This rank's rows of the buffer the next ``start()`` gathers (write them first)."""

@@ -368,16 +368,33 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
             const float4 w4 = *reinterpret_cast<const float4*>(cws + j);
             float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
             if (HAS_BIAS) b4 = *reinterpret_cast<const float4*>(cbs + j);
-            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-            const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
             float r[4];
+            if (HAS_BIAS) {
+              // Scalar: a paired multiply followed by a paired add may be
+              // contracted into one fma, which would round once.
+              const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+              const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              float v = __int2float_rn(static_cast<int>(acc[j + u]));
-              v = __fmul_rn(v, xs);
-              v = __fmul_rn(v, wv[u]);
-              if (HAS_BIAS) v = __fadd_rn(v, bv[u]);
-              r[u] = v;
+              for (int u = 0; u < 4; ++u) {
+                float v = __int2float_rn(static_cast<int>(acc[j + u]));
+                v = __fmul_rn(v, xs);
+                v = __fmul_rn(v, wv[u]);
+                r[u] = __fadd_rn(v, bv[u]);
+              }
+            } else {
+              // Two columns per paired multiply: each lane one IEEE rounding,
+              // as the scalar (float(acc) * xs) * ws.
+              const float2 xs2 = make_float2(xs, xs);
+              float2 r01 = make_float2(__int2float_rn(static_cast<int>(acc[j])),
+                                       __int2float_rn(static_cast<int>(acc[j + 1])));
+              float2 r23 = make_float2(__int2float_rn(static_cast<int>(acc[j + 2])),
+                                       __int2float_rn(static_cast<int>(acc[j + 3])));
+              r01 = mul2(mul2(r01, xs2), make_float2(w4.x, w4.y));
+              r23 = mul2(mul2(r23, xs2), make_float2(w4.z, w4.w));
+              r[0] = r01.x;
+              r[1] = r01.y;
+              r[2] = r23.x;
+              r[3] = r23.y;
             }
             if (OUT == 0) {
 #pragma unroll

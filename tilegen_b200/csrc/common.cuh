@@ -213,6 +213,14 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// After tmem_wait_ld: the compiler treats these registers as written here, so
+// no use of them can be moved above the wait (emits no instruction).
+template <int N>
+__device__ __forceinline__ void reg_after_wait(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane
 // (base lane + i), columns [col, col+32).
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {

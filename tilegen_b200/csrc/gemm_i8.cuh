@@ -332,22 +332,15 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       const float xs = row < p.M ? p.xscale[row] : 0.0f;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(ab * BN_MAX);
 
-#pragma unroll 1
-      for (int ch = 0; ch < NCH; ++ch) {
-        uint32_t acc[CH];
+      // One chunk of columns: tcgen05.ld of 32 lanes x CH columns, dequantise,
+      // stage, TMA store.  The next chunk's tensor-memory load is issued before
+      // this chunk is converted, so its latency overlaps the conversion.
+      auto load_chunk = [&](uint32_t (&acc)[CH], int ch) {
 #pragma unroll
         for (int h = 0; h < CH / 32; ++h)
           tmem_ld_32x32b_x32(t_row + uint32_t(ch * CH + h * 32), *reinterpret_cast<uint32_t(*)[32]>(&acc[h * 32]));
-        tmem_wait_ld();
-        if (ch == NCH - 1) {
-          // This warp is done reading the accumulator: hand it back to the MMA.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if (PAIR) mbar_arrive_cluster(ab ? tempty_leader1 : tempty_leader0);
-            else mbar_arrive(&tempty_bar[ab]);
-          }
-        }
+      };
+      auto store_chunk = [&](const uint32_t (&acc)[CH], int ch) {
         // The TMA store that last used this staging chunk (NBUF chunks ago)
         // must have finished reading it; later stores may still be in flight.
         uint8_t* const sbuf = sbufs + (chunk_seq % NBUF) * OUT_BYTES;
@@ -426,6 +419,27 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
             tma_store_2d(&tma_out, sbuf, n0 + ch * CH, m0 + quarter * 32);
           bulk_commit();
         }
+      };
+      uint32_t acc_a[CH], acc_b[CH];
+      load_chunk(acc_a, 0);
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        uint32_t(&cur)[CH] = (ch & 1) ? acc_b : acc_a;
+        uint32_t(&nxt)[CH] = (ch & 1) ? acc_a : acc_b;
+        tmem_wait_ld();
+        reg_after_wait(cur);
+        if (ch + 1 < NCH) {
+          load_chunk(nxt, ch + 1);
+        } else {
+          // This warp is done reading the accumulator: hand it back to the MMA.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (PAIR) mbar_arrive_cluster(ab ? tempty_leader1 : tempty_leader0);
+            else mbar_arrive(&tempty_bar[ab]);
+          }
+        }
+        store_chunk(cur, ch);
       }
     }
     if (lane == 0) bulk_wait<0>();

@@ -63,9 +63,13 @@ const char *tg_status_string(int status);
  *          K must be a multiple of 256 and at most tg_rotate_quant_max_k()
  *   q      [M, K] int8 out: clamp(rint(rot * 1/(sqrt(G)*scale)), -128, 127)
  *   scale  [M] fp32 out:   max(absmax(rot_unnormalised) / (127*sqrt(G)), 1e-30)
- * The rotation is evaluated in fp32 in the reference kernel's butterfly order,
- * so the result is bit-identical to it for fp16 input; bf16 is read directly
- * (the reference first casts bf16 to fp16, int8_convrot.py:204-206).
+ * The rotation is evaluated in fp32 in a short butterfly order (each output
+ * S - 2*a_i with S the sum of the butterfly's four inputs, one fma) and, for
+ * rows whose rotated values are all finite, rint(rot * inv) as one fma: codes
+ * may differ from the reference kernel's by one at rounding ties (about 1e-6
+ * of them on DiT activations), scales by a few ulps.  tg_quantize_act with
+ * TG_QUANT_REFERENCE_ORDER gives the reference kernel's bits.  bf16 is read
+ * directly (the reference first casts bf16 to fp16, int8_convrot.py:204-206).
  * M == 0 is a no-op.
  */
 int tg_rotate_quant(const void *x, int x_dtype, int64_t M, int64_t K, int group, int8_t *q, float *scale,

@@ -2,11 +2,17 @@
 //
 // Algorithm (the reference kernel `fht_quant`, tilegen/kernels/int8_convrot.py:47-104):
 // per group of G = 4^NST elements, NST radix-4 butterfly stages on the H4 of
-// tilegen/kernels/hadamard.py:15, stage s at stride 4^s, every output summed left
-// to right as at int8_convrot.py:74-77; then the row absmax, the scale
-// absmax/(127*sqrt(G)) clamped at 1e-30, and codes rint(v / (sqrt(G)*scale)).
-// The same fp32 operations in the same order make the codes and scales
-// bit-identical to that kernel (and to the C oracle that restates it).
+// tilegen/kernels/hadamard.py:15, stage s at stride 4^s; then the row absmax,
+// the scale absmax/(127*sqrt(G)) clamped at 1e-30, and codes
+// rint(v / (sqrt(G)*scale)).  Two fp32 evaluation orders (EXACT):
+//  * EXACT: every output summed left to right as at int8_convrot.py:74-77, the
+//    product rounded and clamped: the same operations in the same order, so
+//    codes and scales are bit-identical to that kernel (and to the C oracle's
+//    oracle_rotate_quant);
+//  * short (the default): each output S - 2*a_i in one fma (bfly4x2_short) and
+//    the code rint(v*inv) as one fma for finite rows: fewer roundings, codes
+//    within one of the reference order's at rounding ties (bit-identical to the
+//    oracle's oracle_rotate_quant_short).
 //
 // B200 layout:
 //  * A persistent CTA owns R rows at a time ("a batch").  One thread owns one

@@ -239,3 +239,22 @@ def test_registry_rule_on_cuda_inputs(cuda, fake_kitchen, monkeypatch):
     assert rule(big).failed_param == "x"
     monkeypatch.setattr(backend, "_FAILED_FHT_SHAPES", {(4, 5120, torch.float16, cuda.index or 0)})
     assert rule(x).failed_param == "x"
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_rowwise_and_fused_act_at_the_dit_block_size(cuda, dtype):
+    """65520 rows (the DiT block's 2 x 32760 tokens on one GPU), K=5120: each
+    persistent CTA turns its ring hundreds of times.  Row-wise: bit-identical to
+    torch's evaluation on the GPU and to the oracle; fused gelu_tanh + rotation:
+    bit-identical to torch's GELU followed by the quantiser."""
+    x = outlier_activations(65520, 5120, seed=31, dtype=dtype, device=cuda)
+    q, s = ops.quantize_act(x, 1, None)
+    rq, rs = _torch_rowwise(x)
+    torch.cuda.synchronize()
+    _assert_same(q, s, rq, rs, "row-wise at 65520 rows")
+    oq, os_ = oracle.rowwise_quant(raw16(x), DT_NAME[dtype])
+    assert np.array_equal(q.cpu().numpy(), oq) and np.array_equal(s.cpu().numpy(), os_)
+    fq, fs = ops.quantize_act(x, 256, "gelu_tanh")
+    uq, us = ops.rotate_quant(F.gelu(x, approximate="tanh"), 256)
+    torch.cuda.synchronize()
+    _assert_same(fq, fs, uq, us, "fused gelu_tanh at 65520 rows")

@@ -386,12 +386,37 @@ def _shape_table(dev, flush, stream, iters=100):
     return rows
 
 
-def _quant_sweep(dev, flush, stream, iters=10):
-    """Standalone rotate+quant over group x K x M x dtype (inputs N(0,1), 1 % outlier
-    channels x30): per entry [group, K, M, dtype, us, GB/s, fraction of HBM peak]."""
+def _stream_us(fn_for, bufs, stream, reps=5):
+    """Per-launch microseconds of ``fn_for(buf)`` run back to back over ``bufs`` (whose
+    total is larger than L2, so every launch reads its input from HBM), between two
+    events; median over ``reps`` passes."""
     import torch
 
-    from tilegen_b200 import ops
+    for b in bufs:
+        fn_for(b)
+    out = []
+    for _ in range(reps):
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for b in bufs:
+            fn_for(b)
+        e.record(stream)
+        torch.cuda.synchronize()
+        out.append(a.elapsed_time(e) * 1e3 / len(bufs))
+    return statistics.median(out)
+
+
+def _quant_sweep(dev, flush, stream, iters=10):
+    """Standalone rotate+quant over group x K x M x dtype (inputs N(0,1), 1 % outlier
+    channels x30): per entry [group, K, M, dtype, us, GB/s, fraction of HBM peak,
+    us_stream, fraction_stream].  ``us`` is one launch between two events after an L2
+    flush, which includes the fixed cost of an event-timed launch; ``us_stream`` (M =
+    4096) is the per-launch time of launches back to back (through the C ABI, outputs
+    allocated beforehand) over enough input buffers that together exceed twice the L2,
+    so each launch still reads its input from HBM."""
+    import torch
+
+    from tilegen_b200 import _lib, ops
     from tilegen_b200.synthetic import outlier_activations
 
     hbm = _peaks()[0]["hbm_gbs"]
@@ -413,9 +438,31 @@ def _quant_sweep(dev, flush, stream, iters=10):
                     for _ in range(2):
                         f([torch.cuda.Event(enable_timing=True) for _ in range(2)])
                     us = statistics.median(r[0] for r in _time_steps(f, iters, flush, stream)) * 1e3
-                    gbs = (m * k * 3 + 4 * m) / (us * 1e-6) / 1e9
-                    rows.append([group, k, m, "fp16" if dt == torch.float16 else "bf16", round(us, 2),
-                                 round(gbs, 1), round(gbs / hbm, 4)])
+                    byts = m * k * 3 + 4 * m
+                    gbs = byts / (us * 1e-6) / 1e9
+                    row = [group, k, m, "fp16" if dt == torch.float16 else "bf16", round(us, 2),
+                           round(gbs, 1), round(gbs / hbm, 4), None, None]
+                    if m == 4096:
+                        # Straight through the C ABI with outputs allocated up front,
+                        # so the host issues launches faster than the GPU runs them.
+                        nbuf = max(2, -(-(256 << 20) // (m * k * 2)))
+                        bufs = [x] + [outlier_activations(m, k, seed=j + 1, dtype=dt, device=dev)
+                                      for j in range(nbuf - 1)]
+                        outs = [(torch.empty((m, k), dtype=torch.int8, device=dev),
+                                 torch.empty((m,), dtype=torch.float32, device=dev)) for _ in bufs]
+                        L = _lib.lib()
+                        code = _lib.TG_DT_F16 if dt == torch.float16 else _lib.TG_DT_BF16
+                        calls = [(b.data_ptr(), o[0].data_ptr(), o[1].data_ptr()) for b, o in zip(bufs, outs)]
+
+                        def launch(c):
+                            _lib.check("tg_quantize_act", L.tg_quantize_act(
+                                c[0], code, m, k, group, _lib.TG_ACT_NONE, c[1], c[2], stream.cuda_stream))
+
+                        us_s = _stream_us(launch, calls, stream)
+                        row[7] = round(us_s, 2)
+                        row[8] = round(byts / (us_s * 1e-6) / 1e9 / hbm, 4)
+                        del bufs, outs
+                    rows.append(row)
                     del x
     return rows
 
@@ -835,7 +882,8 @@ def run_tilegen(args):
         line["dit_shapes"] = shapes
     line["dit_block_bf16"] = {"tokens": 65520, "rows_sharded_over": world, "shapes": block}
     if sweep is not None:
-        line["quant_sweep"] = {"columns": ["group", "K", "M", "dtype", "us", "GB/s", "frac_of_hbm"], "rows": sweep}
+        line["quant_sweep"] = {"columns": ["group", "K", "M", "dtype", "us", "GB/s", "frac_of_hbm", "us_stream",
+                                           "frac_of_hbm_stream"], "rows": sweep}
     if gather is not None:
         line["gather_rows"] = gather
     if act_table is not None:

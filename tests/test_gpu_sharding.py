@@ -129,3 +129,84 @@ def test_peer_copy_gather_equals_single_gpu(m):
             pytest.fail("a rank hung")
     res = sorted(q.get(timeout=10) for _ in procs)
     assert all(r[1] for r in res), res
+
+
+def _peer_one_gpu_worker(rank, world, port, fail_rank, q):
+    """Both ranks on cuda:0 with gloo (host-side collectives): the copy-engine gather's
+    protocol and buffers without a second GPU.  ``fail_rank`` >= 0 makes that rank's
+    buffer allocation fail, and every rank must then raise, none may hang."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from tilegen_b200 import _lib
+    from tilegen_b200.sharding import PeerRowGather, shard_bounds
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    g = None
+    try:
+        m, n = 1000, 256
+        if rank == fail_rank:
+            real = _lib.lib()
+
+            class _Failing:
+                def __getattr__(self, name):
+                    if name == "tg_peer_alloc":
+                        return lambda *a: _lib.TG_ERR_CUDA
+                    return getattr(real, name)
+
+            orig = _lib.lib
+            _lib.lib = lambda: _Failing()
+        try:
+            g = PeerRowGather(m, n, torch.bfloat16, dev)
+        finally:
+            if rank == fail_rank:
+                _lib.lib = orig
+        ok = True
+        for step in range(3):
+            full = torch.randn(m, n, generator=torch.Generator().manual_seed(step)).to(torch.bfloat16).to(dev)
+            s, e = shard_bounds(m, world, rank)
+            g.local().copy_(full[s:e])
+            y = g.start().wait()
+            torch.cuda.synchronize()
+            ok = ok and bool(torch.equal(y, full))
+        q.put((rank, "ok" if ok else "mismatch"))
+    except RuntimeError as e:
+        q.put((rank, "raised" if "PeerRowGather" in str(e) else f"other: {e}"[:200]))
+    except Exception as e:  # report, never hang
+        q.put((rank, f"{type(e).__name__}: {e}"[:200]))
+    finally:
+        if g is not None:
+            g.close()
+        dist.destroy_process_group()
+
+
+def _run_one_gpu(fail_rank):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_one_gpu_worker, args=(r, 2, port, fail_rank, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung")
+    return sorted(q.get(timeout=10) for _ in procs)
+
+
+def test_peer_gather_protocol_on_one_gpu():
+    """Two processes on one GPU: three steps over both buffers equal the full rows."""
+    res = _run_one_gpu(-1)
+    assert [r[1] for r in res] == ["ok", "ok"], res
+
+
+def test_peer_gather_setup_failure_raises_on_every_rank():
+    """A rank whose buffer allocation fails: both ranks raise (no hang)."""
+    res = _run_one_gpu(1)
+    assert [r[1] for r in res] == ["raised", "raised"], res

@@ -204,6 +204,20 @@ int tg_gemm_config(int64_t M, int64_t N, int *bn, int *pair);
 int tg_set_gemm_config(int bn, int pair);
 
 /*
+ * Cap the SMs the persistent kernels (tg_rotate_quant / tg_quantize_act and
+ * tg_int8_gemm_dequant) size their grids for, in every later call of this
+ * process: sms = 0 lifts the cap.  They normally take every SM, so a kernel
+ * running at the same time on another stream (an NCCL collective, say) that
+ * holds even one SM keeps part of their grid from starting until it ends;
+ * with the SMs that kernel needs left out, both run at once.  No reference
+ * counterpart.  TG_ERR_INVALID_ARG for sms < 0.
+ */
+int tg_set_sm_budget(int sms);
+
+/* The current cap (0 = none). */
+int tg_sm_budget(void);
+
+/*
  * Read (and optionally clear) the device status word of `device`, which
  * kernels set when a bounded wait expires.  Synchronises the device.
  * *bits receives the raw word (0 = healthy); returns TG_ERR_DEVICE_TIMEOUT when

@@ -131,3 +131,17 @@ def test_splitk_config_checks_arguments():
         assert L.tg_int8_gemm_dequant_splitk_config(*args, ctypes.byref(sl), ctypes.byref(cl)) == \
             _lib.TG_ERR_INVALID_ARG
     assert L.tg_int8_gemm_dequant_splitk_config(4, 64, 64, 1, 0, None, None) == _lib.TG_ERR_INVALID_ARG
+
+
+def test_sm_budget_roundtrip():
+    L = _lib.lib()
+    assert L.tg_sm_budget() == 0
+    assert L.tg_set_sm_budget(-1) == _lib.TG_ERR_INVALID_ARG
+    from tilegen_b200 import ops
+
+    with ops.sm_budget(100):
+        assert L.tg_sm_budget() == 100
+        with ops.sm_budget(64):
+            assert L.tg_sm_budget() == 64
+        assert L.tg_sm_budget() == 100
+    assert L.tg_sm_budget() == 0

@@ -130,6 +130,9 @@ def lib() -> ctypes.CDLL:
         L.tg_peer_close.restype = i32
         L.tg_copy_async.argtypes = [p, p, ctypes.c_size_t, p]
         L.tg_copy_async.restype = i32
+        L.tg_set_sm_budget.argtypes = [i32]
+        L.tg_set_sm_budget.restype = i32
+        L.tg_sm_budget.restype = i32
         _lib = L
     return _lib
 

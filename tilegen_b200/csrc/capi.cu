@@ -3,6 +3,7 @@
 // One translation unit holds every kernel so they share the device status word.
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -33,8 +34,13 @@ EncodeTiledFn encode_fn() {
 }
 
 struct DeviceInfo {
-  int sms = 0;
+  int sms = 0;       // SMs the persistent kernels may use (the SM budget applied)
+  int sms_all = 0;   // SMs of the device
 };
+
+// Process-wide cap on the SMs the persistent kernels (rotate+quant, the tiled
+// GEMM) size their grids for; 0 = every SM (tg_set_sm_budget).
+std::atomic<int> g_sm_budget{0};
 
 bool current_device(int* dev, DeviceInfo* info) {
   static DeviceInfo cache[kMaxDevices];
@@ -43,8 +49,11 @@ bool current_device(int* dev, DeviceInfo* info) {
     int v = 0;
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, *dev) != cudaSuccess) return false;
     cache[*dev].sms = v;
+    cache[*dev].sms_all = v;
   }
   *info = cache[*dev];
+  const int budget = g_sm_budget.load(std::memory_order_relaxed);
+  if (budget > 0 && budget < info->sms) info->sms = budget;
   return true;
 }
 
@@ -385,7 +394,9 @@ int launch_gemm_mode(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const
 int gemm_units(int dev, int sms, bool pair) {
   static int cache[kMaxDevices];
   if (!pair) return sms;
-  if (cache[dev] > 0) return cache[dev];
+  if (cache[dev] > 0) return cache[dev] < sms / 2 ? cache[dev] : sms / 2;
+  int all = sms;
+  if (cudaDeviceGetAttribute(&all, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) all = sms;
   auto kern = tg::gemm_i8_dequant_kernel<256, 1, false, true>;
   constexpr uint32_t smem = tg::gemm::smem_bytes(256, true);
   static uint32_t attr_done[kMaxDevices];
@@ -393,7 +404,7 @@ int gemm_units(int dev, int sms, bool pair) {
   if (ensure_smem_attr(kern, dev, smem, attr_done)) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
-    cfg.gridDim = dim3(unsigned(sms));
+    cfg.gridDim = dim3(unsigned(all));
     cfg.blockDim = dim3(tg::gemm::THREADS);
     cfg.dynamicSmemBytes = smem;
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -404,8 +415,8 @@ int gemm_units(int dev, int sms, bool pair) {
     cfg.numAttrs = 1;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
   }
-  cache[dev] = n > 0 ? n : sms / 2;
-  return cache[dev];
+  cache[dev] = n > 0 ? n : all / 2;
+  return cache[dev] < sms / 2 ? cache[dev] : sms / 2;
 }
 
 // Tile shape for an M x N problem.  The persistent grid runs
@@ -500,6 +511,14 @@ int tg_int8_gemm_dequant(const int8_t* xq, const float* xscale, const int8_t* wq
   return pair ? launch_gemm_mode<true>(bn, ta, tb, to, p, out_dtype, hb, dev, units, st)
               : launch_gemm_mode<false>(bn, ta, tb, to, p, out_dtype, hb, dev, units, st);
 }
+
+int tg_set_sm_budget(int sms) {
+  if (sms < 0) return TG_ERR_INVALID_ARG;
+  g_sm_budget.store(sms, std::memory_order_relaxed);
+  return TG_OK;
+}
+
+int tg_sm_budget(void) { return g_sm_budget.load(std::memory_order_relaxed); }
 
 int tg_set_gemm_config(int bn, int pair) {
   if (pair < -1 || pair > 1) return TG_ERR_INVALID_ARG;

@@ -14,6 +14,8 @@ as opaque ops).
 """
 from __future__ import annotations
 
+import contextlib
+
 import torch
 
 from . import _lib
@@ -184,6 +186,21 @@ def int8_gemm_dequant(xq: torch.Tensor, xscale: torch.Tensor, wq: torch.Tensor, 
         _call("tg_int8_gemm_dequant", dev, xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),
               ws.numel(), b_ptr, b_code, m, n, k, _DTYPE_CODE[out_dtype], out.data_ptr())
     return out
+
+
+@contextlib.contextmanager
+def sm_budget(sms: int):
+    """Within the block, the persistent kernels (rotate+quant, the tiled GEMM) size their
+    grids for at most ``sms`` SMs (``tg_set_sm_budget``; process-wide, restored on
+    exit).  Use it for kernels that run while a collective is in flight on another
+    stream, leaving that collective the SMs it occupies, so both proceed at once."""
+    L = _lib.lib()
+    old = int(L.tg_sm_budget())
+    _lib.check("tg_set_sm_budget", L.tg_set_sm_budget(int(sms)))
+    try:
+        yield
+    finally:
+        L.tg_set_sm_budget(old)
 
 
 # Largest M int8_gemm_dequant sends to the split-K kernel

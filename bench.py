@@ -596,12 +596,24 @@ def _gather_table(dev, flush, stream, world, rank, tokens=65520, iters=10):
         nxt()
         e[1].record(stream)
 
-    def overlapped(e):
-        e[0].record(stream)
-        pending = gather_rows(y, tokens, async_op=True)
-        nxt()
-        pending.wait()
-        e[1].record(stream)
+    # The persistent kernels normally take every SM; a collective in flight holds
+    # some, which would keep part of their grid waiting until it ends.  While a
+    # gather runs, the next layer leaves it SMs: NCCL's all-gather kernels
+    # (about one CTA per channel), or 2 for the copy-engine gather's one-element
+    # all-reduce.
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+
+    def overlapped_with(reserve):
+        def f(e):
+            e[0].record(stream)
+            pending = gather_rows(y, tokens, async_op=True)
+            with ops.sm_budget(sms - reserve if reserve else 0):
+                nxt()
+            pending.wait()
+            e[1].record(stream)
+        return f
+
+    overlapped = overlapped_with(0)
 
     def next_only(e):
         e[0].record(stream)
@@ -636,12 +648,14 @@ def _gather_table(dev, flush, stream, world, rank, tokens=65520, iters=10):
     def ce_overlapped(e):
         e[0].record(stream)
         pending = pg.start()
-        nxt()
+        with ops.sm_budget(sms - 2):
+            nxt()
         pending.wait()
         e[1].record(stream)
 
     res = []
-    fns = (gather_only, next_only, serial, overlapped) + ((ce_only, ce_serial, ce_overlapped) if pg else ())
+    fns = (gather_only, next_only, serial, overlapped, overlapped_with(16), overlapped_with(32)) + \
+        ((ce_only, ce_serial, ce_overlapped) if pg else ())
     for fn in fns:
         for _ in range(3):
             fn([torch.cuda.Event(enable_timing=True) for _ in range(2)])
@@ -656,19 +670,23 @@ def _gather_table(dev, flush, stream, world, rank, tokens=65520, iters=10):
     t = torch.tensor(res, device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dist.all_reduce(same, op=dist.ReduceOp.MIN)
-    g, nx, se, ov = (float(v) for v in t[:4])
+    g, nx, se, ov, ov16, ov32 = (float(v) for v in t[:6])
     per = -(-tokens // world)
     moved = (world - 1) * per * 5120 * 2  # bytes each rank receives
     out = {"tokens": tokens, "N": 5120, "dtype": "fp16", "gather_us": round(g, 1),
            "gather_bus_gbs": round(moved / (g * 1e-6) / 1e9, 1), "next_layer": "ffn_up on the local rows",
            "next_layer_us": round(nx, 1), "gather_then_next_us": round(se, 1),
-           "gather_overlapped_with_next_us": round(ov, 1)}
+           "gather_overlapped_with_next_us": round(ov, 1),
+           "gather_overlapped_next_on_fewer_sms_us": {"16 SMs left to NCCL": round(ov16, 1),
+                                                     "32 SMs left to NCCL": round(ov32, 1)}}
     if pg is None:
         out["copy_engine"] = {"error": pg_error}
         return out
-    ce, ces, ceo = (float(v) for v in t[4:])
+    ce, ces, ceo = (float(v) for v in t[6:])
     out["copy_engine"] = {"gather_us": round(ce, 1), "gather_bus_gbs": round(moved / (ce * 1e-6) / 1e9, 1),
-                          "gather_then_next_us": round(ces, 1), "gather_overlapped_with_next_us": round(ceo, 1),
+                          "gather_then_next_us": round(ces, 1),
+                          "gather_overlapped_with_next_us": round(ceo, 1),
+                          "overlap_note": "the next layer on all SMs but 2 (ops.sm_budget)",
                           "equal_to_nccl_gather": bool(same.item() == 1.0),
                           "path": "tilegen_b200.sharding.PeerRowGather: a one-element NCCL all-reduce as the "
                                   "ready signal, then one cudaMemcpyAsync per peer from its mapped buffer, "

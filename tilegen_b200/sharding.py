@@ -7,7 +7,12 @@ no collective on the path.  When a caller needs the full ``[M, N]`` output on
 every rank, ``gather_rows`` all-gathers the blocks over NCCL (NVLink), as one
 collective outside the hot path; with ``async_op=True`` it returns at once and
 the caller overlaps the transfer with the next layer's kernels, waiting only
-where the gathered output is used.
+where the gathered output is used.  The rotate+quant and GEMM kernels are
+persistent and size their grids for every SM, so run the next layer under
+``ops.sm_budget(sms - reserve)`` while a gather is in flight, leaving the
+collective's kernels the SMs they hold (NCCL's all-gather: about one CTA per
+channel, 32 SMs; the copy-engine gather below: 2); otherwise part of the
+next layer's grid waits for the collective to finish.
 
 Blocks are ``ceil(M / world)`` rows; the last rank's block may be short or
 empty.  ``gather_rows`` pads the short blocks to the common size for the
@@ -127,7 +132,8 @@ class PeerRowGather:
        several copy engines run at once; nothing waits on the host;
     3. ``wait()`` on the returned handle (the caller's current stream waits for the
        copies) gives the full output.  Kernels enqueued between ``start()`` and
-       ``wait()`` overlap the transfer and keep every SM.
+       ``wait()`` overlap the transfer; run them under ``ops.sm_budget(sms - 2)``
+       so that the one-element all-reduce finds an SM.
 
     The two buffers alternate between steps, so a step's rows may be written while
     peers may still copy the previous step's.  Call ``wait()`` on one step's gather

@@ -80,6 +80,10 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
+    # NVML clocks-event reason bits (nvml.h): SW power cap, HW slowdown, SW thermal, HW thermal.
+    NVML_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+                    0x40: "hw_thermal_slowdown"}
+
     def __init__(self, gpu_index: int):
         vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
         if 0 <= gpu_index < len(vis) and vis[gpu_index].strip().isdigit():
@@ -87,6 +91,20 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self._nvml = None
+        self._thread = None
+        self._stop = False
+        self._samples = []  # (sm MHz, reason bits) read by NVML during the with-block
+
+    def _poll(self, nvml, handle):
+        while not self._stop:
+            try:
+                mhz = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                bits = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                self._samples.append((float(mhz), int(bits)))
+            except Exception:
+                return
+            time.sleep(0.0005)
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
@@ -98,9 +116,26 @@ class ClockSampler:
             time.sleep(0.3)
         except Exception:
             self.proc = None
+        # NVML read every ~0.5 ms while the with-block (the timed region, a few ms)
+        # runs: nvidia-smi's 100 ms period may not fall inside it at all.
+        try:
+            import threading
+
+            import pynvml
+
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self._nvml = pynvml
+            self._thread = threading.Thread(target=self._poll, args=(pynvml, handle), daemon=True)
+            self._thread.start()
+        except Exception:
+            self._thread = None
         return self
 
     def __exit__(self, *a):
+        self._stop = True
+        if self._thread is not None:
+            self._thread.join(5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -109,6 +144,18 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if self._samples:
+            smax = None
+            try:
+                h = self._nvml.nvmlDeviceGetHandleByIndex(self.gpu)
+                smax = float(self._nvml.nvmlDeviceGetMaxClockInfo(h, self._nvml.NVML_CLOCK_SM))
+            except Exception:
+                pass
+            reasons = sorted({nm for _, bits in self._samples for b, nm in self.NVML_REASONS.items() if bits & b})
+            if self.path and os.path.exists(self.path):
+                os.unlink(self.path)
+            return {"sm_mhz": statistics.median(m for m, _ in self._samples), "sm_max_mhz": smax,
+                    "samples": len(self._samples), "source": "NVML during the timed region", "reasons": reasons}
         if not self.path or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm, smax, reasons = [], None, set()
@@ -127,7 +174,7 @@ class ClockSampler:
                     reasons.add(nm)
         os.unlink(self.path)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
-                "reasons": sorted(reasons)}
+                "source": "nvidia-smi", "reasons": sorted(reasons)}
 
 
 # ------------------------------------------------------------------ helpers

@@ -645,9 +645,9 @@ def _gather_table(dev, flush, stream, world, rank, tokens=65520, iters=10):
 
     # The persistent kernels normally take every SM; a collective in flight holds
     # some, which would keep part of their grid waiting until it ends.  While a
-    # gather runs, the next layer leaves it SMs: NCCL's all-gather kernels
-    # (about one CTA per channel), or 2 for the copy-engine gather's one-element
-    # all-reduce.
+    # gather runs, the next layer leaves it SMs: NCCL's all-gather kernels (on
+    # B200 with NCCL 2.28 they hold about 32 SMs at 2 GPUs and 64 at 8), or 2 for
+    # the copy-engine gather's one-element all-reduce.
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
 
     def overlapped_with(reserve):
@@ -701,7 +701,7 @@ def _gather_table(dev, flush, stream, world, rank, tokens=65520, iters=10):
         e[1].record(stream)
 
     res = []
-    fns = (gather_only, next_only, serial, overlapped, overlapped_with(16), overlapped_with(32)) + \
+    fns = (gather_only, next_only, serial, overlapped, overlapped_with(32), overlapped_with(64)) + \
         ((ce_only, ce_serial, ce_overlapped) if pg else ())
     for fn in fns:
         for _ in range(3):
@@ -717,15 +717,16 @@ def _gather_table(dev, flush, stream, world, rank, tokens=65520, iters=10):
     t = torch.tensor(res, device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dist.all_reduce(same, op=dist.ReduceOp.MIN)
-    g, nx, se, ov, ov16, ov32 = (float(v) for v in t[:6])
+    g, nx, se, ov, ov32, ov64 = (float(v) for v in t[:6])
     per = -(-tokens // world)
     moved = (world - 1) * per * 5120 * 2  # bytes each rank receives
     out = {"tokens": tokens, "N": 5120, "dtype": "fp16", "gather_us": round(g, 1),
            "gather_bus_gbs": round(moved / (g * 1e-6) / 1e9, 1), "next_layer": "ffn_up on the local rows",
            "next_layer_us": round(nx, 1), "gather_then_next_us": round(se, 1),
            "gather_overlapped_with_next_us": round(ov, 1),
-           "gather_overlapped_next_on_fewer_sms_us": {"16 SMs left to NCCL": round(ov16, 1),
-                                                     "32 SMs left to NCCL": round(ov32, 1)}}
+           "gather_overlapped_next_on_fewer_sms_us": {"32 SMs left to NCCL": round(ov32, 1),
+                                                     "64 SMs left to NCCL": round(ov64, 1)},
+           "gather_overlapped_best_us": round(min(ov, ov32, ov64), 1)}
     if pg is None:
         out["copy_engine"] = {"error": pg_error}
         return out

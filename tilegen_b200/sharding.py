@@ -10,9 +10,9 @@ the caller overlaps the transfer with the next layer's kernels, waiting only
 where the gathered output is used.  The rotate+quant and GEMM kernels are
 persistent and size their grids for every SM, so run the next layer under
 ``ops.sm_budget(sms - reserve)`` while a gather is in flight, leaving the
-collective's kernels the SMs they hold (NCCL's all-gather: about one CTA per
-channel, 32 SMs; the copy-engine gather below: 2); otherwise part of the
-next layer's grid waits for the collective to finish.
+collective's kernels the SMs they hold (NCCL 2.28's all-gather on B200: about
+32 SMs at 2 GPUs, 64 at 8; the copy-engine gather below: 2); otherwise part of
+the next layer's grid waits for the collective to finish.
 
 Blocks are ``ceil(M / world)`` rows; the last rank's block may be short or
 empty.  ``gather_rows`` pads the short blocks to the common size for the

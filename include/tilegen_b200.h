@@ -6,9 +6,9 @@
  *     (NULL = the legacy default stream) and only enqueues work on it: no host
  *     synchronisation, no allocation;
  *   - returns a tg_status; nothing is launched when it is not TG_OK.
- * tg_rotate_quant, tg_quantize_act, tg_int8_gemm_dequant and
- * tg_int8_gemm_dequant_splitk work only on buffers the caller owns, so they
- * can be captured in CUDA graphs.
+ * tg_rotate_quant, tg_quantize_act, tg_int8_gemm_dequant,
+ * tg_int8_gemm_dequant_splitk and tg_int8_gemv_dequant work only on buffers
+ * the caller owns, so they can be captured in CUDA graphs.
  * Device-side failures (a bounded wait that gave up) are recorded in a device
  * status word that tg_device_status() reads.
  *
@@ -161,6 +161,32 @@ int64_t tg_int8_gemm_dequant_splitk_max_m(void);
  */
 int tg_int8_gemm_dequant_splitk_config(int64_t M, int64_t N, int64_t K, int out_dtype, int has_bias, int *slices,
                                        int *cluster);
+
+/* Largest M tg_int8_gemv_dequant accepts. */
+#define TG_GEMV_MAX_M 4
+
+/*
+ * The same GEMM + dequantisation for one to four activation rows, on the CUDA
+ * cores: each warp streams four weight rows (over one part of K) with 128-bit
+ * loads and sums exact int32 dp4a products; a quarter of the weight is asked
+ * into L2 before the wait for the kernel that wrote xq, so the weight stream
+ * starts while that kernel runs.
+ * Bit-identical to tg_int8_gemm_dequant.  Replaces the reference's
+ * `int8_matmul_dequant_chunked` (tilegen/quant/int8_ops.py:22-70) at these M,
+ * where its GEMM is torch._int_mm's.  No workspace and no allocation.
+ *
+ * Arguments as tg_int8_gemm_dequant; TG_ERR_UNSUPPORTED for M > TG_GEMV_MAX_M.
+ */
+int tg_int8_gemv_dequant(const int8_t *xq, const float *xscale, const int8_t *wq, const float *wscale,
+                         int64_t wscale_numel, const void *bias, int bias_dtype, int64_t M, int64_t N, int64_t K,
+                         int out_dtype, void *out, void *stream);
+
+/*
+ * How tg_int8_gemv_dequant runs an N x K weight on the current device:
+ * *parts = warps that split the K of each group of four weight rows (1, 2, 4
+ * or 8), *ctas = its grid.  No reference counterpart (for tests and tuning).
+ */
+int tg_int8_gemv_dequant_config(int64_t N, int64_t K, int *parts, int *ctas);
 
 /*
  * tg_int8_gemm_dequant_splitk for callers that cannot allocate device memory:

@@ -314,6 +314,12 @@ def test_small_m_routing_boundaries():
     assert splitk_route(24, 13824, 5120) and not splitk_route(32, 13824, 5120)      # ffn_up
     assert splitk_route(128, 5120, 13824) and not splitk_route(129, 5120, 13824)    # ffn_down
     assert not splitk_route(0, 5120, 5120) and not splitk_route(4096, 5120, 5120)
+    from tilegen_b200.ops import GEMV_MAX_M, gemv_route
+
+    assert 0 < GEMV_MAX_M <= 4  # tg_int8_gemv_dequant's limit (TG_GEMV_MAX_M)
+    assert gemv_route(1, 15360, 5120) and gemv_route(4, 5120, 5120) and gemv_route(2, 5120, 13824)
+    assert not gemv_route(3, 5120, 13824)                                          # ffn_down: split-K
+    assert not gemv_route(0, 5120, 5120) and not gemv_route(GEMV_MAX_M + 1, 5120, 5120)
 
 
 def test_host_linear_chunk_schedule_covers_rows():

@@ -99,6 +99,25 @@ def test_small_m_entry_points_check_before_device_work():
                                                  None) == _lib.TG_OK
 
 
+def test_gemv_entry_points_check_before_device_work():
+    L = _lib.lib()
+    p = ctypes.c_void_p(256)
+    assert {"tg_int8_gemv_dequant", "tg_int8_gemv_dequant_config"} <= set(_lib.declared_functions())
+    # M above TG_GEMV_MAX_M (4), null operands, misaligned weight, K not a multiple of 16
+    assert L.tg_int8_gemv_dequant(p, p, p, p, 1, None, 0, 5, 128, 64, 1, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_int8_gemv_dequant(None, p, p, p, 1, None, 0, 1, 128, 64, 1, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_int8_gemv_dequant(p, p, ctypes.c_void_p(264), p, 1, None, 0, 1, 128, 64, 1, p, None) == \
+        _lib.TG_ERR_MISALIGNED
+    assert L.tg_int8_gemv_dequant(p, p, p, p, 1, None, 0, 1, 128, 72, 1, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_int8_gemv_dequant(p, p, p, p, 3, None, 0, 1, 128, 64, 1, p, None) == _lib.TG_ERR_INVALID_ARG
+    # M == 0 is a no-op
+    assert L.tg_int8_gemv_dequant(None, None, None, None, 1, None, 0, 0, 128, 64, 1, None, None) == _lib.TG_OK
+    parts, ctas = ctypes.c_int(0), ctypes.c_int(0)
+    assert L.tg_int8_gemv_dequant_config(0, 64, ctypes.byref(parts), ctypes.byref(ctas)) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_int8_gemv_dequant_config(64, 8, ctypes.byref(parts), ctypes.byref(ctas)) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_int8_gemv_dequant_config(64, 64, None, None) == _lib.TG_ERR_INVALID_ARG
+
+
 def test_quantize_act_checks_before_device_work():
     L = _lib.lib()
     p = ctypes.c_void_p(16)

@@ -39,14 +39,15 @@ def _bits(y):
 def _run(case, out_dtype, dev, max_m):
     """int8_gemm_dequant with every M <= max_m on the split-K kernel (0: the tiled kernel)."""
     xq, xs, wq, ws, bias = case
-    route = ops.splitk_route
+    route, gemv = ops.splitk_route, ops.gemv_route
     ops.splitk_route = lambda m, n, k: 0 < m <= max_m
+    ops.gemv_route = lambda m, n, k: False
     try:
         y = ops.int8_gemm_dequant(xq.to(dev), xs.to(dev), wq.to(dev), ws.to(dev),
                                   None if bias is None else bias.to(dev), out_dtype)
         torch.cuda.synchronize()
     finally:
-        ops.splitk_route = route
+        ops.splitk_route, ops.gemv_route = route, gemv
     return y
 
 

@@ -119,6 +119,10 @@ def lib() -> ctypes.CDLL:
         L.tg_int8_gemm_dequant_splitk_config.argtypes = [i64, i64, i64, i32, i32, ctypes.POINTER(i32),
                                                          ctypes.POINTER(i32)]
         L.tg_int8_gemm_dequant_splitk_config.restype = i32
+        L.tg_int8_gemv_dequant.argtypes = [p, p, p, p, i64, p, i32, i64, i64, i64, i32, p, p]
+        L.tg_int8_gemv_dequant.restype = i32
+        L.tg_int8_gemv_dequant_config.argtypes = [i64, i64, ctypes.POINTER(i32), ctypes.POINTER(i32)]
+        L.tg_int8_gemv_dequant_config.restype = i32
         L.tg_peer_handle_bytes.restype = ctypes.c_size_t
         L.tg_peer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(p), p]
         L.tg_peer_alloc.restype = i32
@@ -152,6 +156,14 @@ def splitk_config(m: int, n: int, k: int, out_dtype_code: int = TG_DT_F16, has_b
           lib().tg_int8_gemm_dequant_splitk_config(int(m), int(n), int(k), int(out_dtype_code), int(has_bias),
                                                    ctypes.byref(sl), ctypes.byref(cl)))
     return sl.value, cl.value
+
+
+def gemv_config(n: int, k: int) -> tuple[int, int]:
+    """(K parts per 4-row group, CTAs) of the few-row GEMV for an n x k weight on the current device."""
+    parts, ctas = ctypes.c_int(0), ctypes.c_int(0)
+    check("tg_int8_gemv_dequant_config",
+          lib().tg_int8_gemv_dequant_config(int(n), int(k), ctypes.byref(parts), ctypes.byref(ctas)))
+    return parts.value, ctas.value
 
 
 def gemm_config(m: int, n: int) -> tuple[int, int]:

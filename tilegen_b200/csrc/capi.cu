@@ -9,6 +9,7 @@
 #include "common.cuh"
 #include "gemm_i8.cuh"
 #include "gemm_splitk.cuh"
+#include "gemv_i8.cuh"
 #include "rotquant.cuh"
 
 namespace {
@@ -784,6 +785,109 @@ int tg_int8_gemm_dequant_splitk_config(int64_t M, int64_t N, int64_t K, int out_
 #undef TG_SK_OK
   *slices = s;
   *cluster = cl ? 1 : 0;
+  return TG_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ few-row GEMV
+namespace {
+
+template <int MR, int OUT, bool HAS_BIAS>
+int launch_gemv_t(const tg::GemvParams& p, int ctas, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(unsigned(ctas));
+  cfg.blockDim = dim3(tg::gemv::THREADS);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, tg::gemv_i8_kernel<MR, OUT, HAS_BIAS>, p) != cudaSuccess) return TG_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess ? TG_OK : TG_ERR_CUDA;
+}
+
+template <int MR>
+int launch_gemv_m(const tg::GemvParams& p, int ctas, int out_dtype, bool hb, cudaStream_t st) {
+  switch (out_dtype) {
+    case TG_DT_F32: return hb ? launch_gemv_t<MR, 0, true>(p, ctas, st) : launch_gemv_t<MR, 0, false>(p, ctas, st);
+    case TG_DT_F16: return hb ? launch_gemv_t<MR, 1, true>(p, ctas, st) : launch_gemv_t<MR, 1, false>(p, ctas, st);
+    default: return hb ? launch_gemv_t<MR, 2, true>(p, ctas, st) : launch_gemv_t<MR, 2, false>(p, ctas, st);
+  }
+}
+
+// K parts per group of 4 weight rows: the fewest of 1, 2, 4, 8 that put at
+// least two CTAs (16 warps) per SM on the weight stream, each part keeping
+// at least one 16-byte chunk per lane.
+int gemv_parts(int64_t N, int64_t K, int sms) {
+  using namespace tg::gemv;
+  const int64_t groups = N / R;
+  const int64_t nch = K / 16;
+  int kp = 1;
+  while (kp < WARPS && (groups * kp + WARPS - 1) / WARPS < 2 * int64_t(sms) && nch >= int64_t(64) * kp) kp *= 2;
+  return kp;
+}
+
+// Weights up to this size have a quarter asked into L2 before the wait (the
+// L2 holds 126 MB, so the quarter stays there until it is read); larger ones
+// stream without the prefetch.
+constexpr int64_t kGemvPrefetchMaxBytes = int64_t(256) << 20;
+
+}  // namespace
+
+extern "C" {
+
+int tg_int8_gemv_dequant(const int8_t* xq, const float* xscale, const int8_t* wq, const float* wscale,
+                         int64_t wscale_numel, const void* bias, int bias_dtype, int64_t M, int64_t N, int64_t K,
+                         int out_dtype, void* out, void* stream) {
+  const int chk = check_gemm_args(xq, xscale, wq, wscale, wscale_numel, bias, bias_dtype, M, N, K, out_dtype, out);
+  if (chk != TG_OK || M == 0) return chk;
+  if (M > TG_GEMV_MAX_M) return TG_ERR_UNSUPPORTED;
+  int dev;
+  DeviceInfo info;
+  if (!current_device(&dev, &info)) return TG_ERR_CUDA;
+  using namespace tg::gemv;
+  const int kp = gemv_parts(N, K, info.sms_all);
+  const int64_t nch = K / 16;
+  const int64_t groups = N / R;  // N is a multiple of 4 (16-byte output rows)
+  const int64_t per_cta = WARPS / kp;
+  const int64_t ctas = (groups + per_cta - 1) / per_cta;
+  if (ctas > 0x7fffffff) return TG_ERR_UNSUPPORTED;
+  tg::GemvParams p;
+  p.xq = xq;
+  p.xscale = xscale;
+  p.wq = wq;
+  p.wscale = wscale;
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.wscale_bcast = wscale_numel == 1 ? 1 : 0;
+  p.M = int(M);
+  p.N = int(N);
+  p.K = int(K);
+  p.kp = kp;
+  p.part_chunks = int((nch + kp - 1) / kp);
+  p.prefetch = N * K <= kGemvPrefetchMaxBytes ? 1 : 0;
+  p.out = out;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool hb = bias != nullptr;
+  switch (M) {
+    case 1: return launch_gemv_m<1>(p, int(ctas), out_dtype, hb, st);
+    case 2: return launch_gemv_m<2>(p, int(ctas), out_dtype, hb, st);
+    default: return launch_gemv_m<4>(p, int(ctas), out_dtype, hb, st);
+  }
+}
+
+int tg_int8_gemv_dequant_config(int64_t N, int64_t K, int* parts, int* ctas) {
+  if (N < 1 || K < 16 || !parts || !ctas) return TG_ERR_INVALID_ARG;
+  int dev;
+  DeviceInfo info;
+  if (!current_device(&dev, &info)) return TG_ERR_CUDA;
+  const int kp = gemv_parts(N, K, info.sms_all);
+  const int64_t per_cta = tg::gemv::WARPS / kp;
+  *parts = kp;
+  *ctas = int((N / tg::gemv::R + per_cta - 1) / per_cta);
   return TG_OK;
 }
 

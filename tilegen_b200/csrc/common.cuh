@@ -120,6 +120,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// ---------------------------------------------------------------- dequantisation
+// out = ((float(acc) * xs) * ws) + bias, one rounding per operation (no FMA),
+// stored as OUT (tg_dtype) with round-to-nearest-even: the reference's fp32
+// epilogue (tilegen/quant/int8_ops.py:22-70) for one output element.
+template <int OUT, bool HAS_BIAS>
+__device__ __forceinline__ void store_dequant(char* o, int32_t acc, float xs, float ws, float bs) {
+  float r = __int2float_rn(acc);
+  r = __fmul_rn(r, xs);
+  r = __fmul_rn(r, ws);
+  if (HAS_BIAS) r = __fadd_rn(r, bs);
+  if (OUT == 0) *reinterpret_cast<float*>(o) = r;
+  else if (OUT == 1) *reinterpret_cast<__half*>(o) = __float2half_rn(r);
+  else *reinterpret_cast<__nv_bfloat16*>(o) = __float2bfloat16_rn(r);
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -67,19 +67,6 @@ struct SplitKParams {
   void* out;         // [M, N] of OUT
 };
 
-// out = ((float(acc) * xs) * ws) + bias, one rounding per operation (no FMA),
-// stored as OUT with round-to-nearest-even.
-template <int OUT, bool HAS_BIAS>
-__device__ __forceinline__ void store_dequant(char* o, int32_t acc, float xs, float ws, float bs) {
-  float r = __int2float_rn(acc);
-  r = __fmul_rn(r, xs);
-  r = __fmul_rn(r, ws);
-  if (HAS_BIAS) r = __fadd_rn(r, bs);
-  if (OUT == 0) *reinterpret_cast<float*>(o) = r;
-  else if (OUT == 1) *reinterpret_cast<__half*>(o) = __float2half_rn(r);
-  else *reinterpret_cast<__nv_bfloat16*>(o) = __float2bfloat16_rn(r);
-}
-
 // MPAD: activation rows padded to 16, 32, 64 or 128 (the UMMA N); OUT: tg_dtype;
 // CL: launched with clusters of gridDim.x CTAs (all slices of a column tile).
 template <int MPAD, int OUT, bool HAS_BIAS, bool CL>

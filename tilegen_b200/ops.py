@@ -4,8 +4,10 @@
 caching allocator and enqueue the sm_100a kernels on the current stream of the
 input's device.  They never fall back to another implementation: an input the
 kernels do not handle raises ``ValueError``, a CUDA failure raises
-``TileGenError``.  ``int8_gemm_dequant`` with few rows (see ``SPLITK_MAX_M``)
-uses the split-K kernel and a cached, self-clearing scratch per (device, stream).
+``TileGenError``.  ``int8_gemm_dequant`` with one to ``GEMV_MAX_M`` rows runs the
+few-row GEMV on the CUDA cores; with up to ``SPLITK_MAX_M`` rows (see
+``splitk_route``) the split-K kernel and a cached, self-clearing scratch per
+(device, stream); otherwise the tiled tcgen05 kernel.
 
 The same functions are registered as ``torch.ops.tilegen.rotate_quant``,
 ``torch.ops.tilegen.quantize_act`` and ``torch.ops.tilegen.int8_gemm_dequant``
@@ -177,7 +179,10 @@ def int8_gemm_dequant(xq: torch.Tensor, xscale: torch.Tensor, wq: torch.Tensor, 
           or out.data_ptr() % 16):
         raise ValueError(f"int8_gemm_dequant: out must be a contiguous 16-byte aligned [{m}, {n}] {out_dtype} "
                          f"tensor on {dev}")
-    if m and splitk_route(m, n, k):
+    if m and gemv_route(m, n, k):
+        _call("tg_int8_gemv_dequant", dev, xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),
+              ws.numel(), b_ptr, b_code, m, n, k, _DTYPE_CODE[out_dtype], out.data_ptr())
+    elif m and splitk_route(m, n, k):
         work = _splitk_workspace(dev, m, n)
         _call("tg_int8_gemm_dequant_splitk", dev, xq.data_ptr(), xs.data_ptr(), wq.data_ptr(), ws.data_ptr(),
               ws.numel(), b_ptr, b_code, m, n, k, _DTYPE_CODE[out_dtype], out.data_ptr(), work.data_ptr(),
@@ -201,6 +206,23 @@ def sm_budget(sms: int):
         yield
     finally:
         L.tg_set_sm_budget(old)
+
+
+# Largest M int8_gemm_dequant sends to the few-row GEMV (tg_int8_gemv_dequant,
+# at most 4); 0 sends none there.
+GEMV_MAX_M = 4
+
+
+def gemv_route(m: int, n: int, k: int) -> bool:
+    """Whether an m x n x k product goes to the few-row GEMV (at most GEMV_MAX_M rows).
+
+    Measured on B200 at the DiT shapes against the split-K kernel, whole linears
+    (quantiser + GEMM) replayed from a CUDA graph with L2 flushed before each:
+    the GEMV is faster at M <= 2 everywhere (M = 1: qkv 16.0 vs 21.3 us, o_proj
+    9.2 vs 11.0, ffn_up 15.4 vs 20.8, ffn_down 15.9 vs 18.9) and at M <= 4 for
+    K < 8192; at K = 13824 with 3-4 rows the two are even, and split-K stays.
+    """
+    return 0 < m <= min(GEMV_MAX_M, 4 if k < 8192 else 2)
 
 
 # Largest M int8_gemm_dequant sends to the split-K kernel

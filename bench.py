@@ -569,6 +569,85 @@ def _input_act_table(dev, flush, stream, iters=20):
     return act_rows, rw_rows
 
 
+def _event_floor_us(dev, flush, stream, iters=30):
+    """A one-element fill kernel timed like a single quantiser launch (between two
+    events after an L2 flush): the fixed cost every such measurement carries."""
+    import torch
+
+    sink = torch.empty(1, dtype=torch.float32, device=dev)
+
+    def f(e):
+        e[0].record(stream)
+        sink.zero_()
+        e[1].record(stream)
+
+    for _ in range(3):
+        f([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+    return statistics.median(r[0] for r in _time_steps(f, iters, flush, stream)) * 1e3
+
+
+def _graph_us(fn, flush, reps=10, iters=7):
+    """Microseconds of ``fn`` replayed ``reps`` times from one CUDA graph, L2 flushed
+    before each (cold weights, as in a model, and no launch gaps), less the same
+    graph of flushes alone; median of ``iters``."""
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+        flush.zero_()
+    torch.cuda.current_stream().wait_stream(s)
+    graphs = []
+    for with_fn in (True, False):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                flush.zero_()
+                if with_fn:
+                    fn()
+        graphs.append(g)
+    out = []
+    for _ in range(iters):
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record()
+        graphs[0].replay()
+        b.record()
+        graphs[1].replay()
+        c.record()
+        torch.cuda.synchronize()
+        out.append((a.elapsed_time(b) - b.elapsed_time(c)) * 1e3 / reps)
+    del graphs
+    return statistics.median(out)
+
+
+def _small_m_table(dev, flush, hbm_gbs):
+    """Few-row linears (decode / preview steps): the routed int8 linear (rotate+quant,
+    then the GEMV, split-K or tiled kernel that ``ops`` picks) against bf16 cuBLAS,
+    both as whole linears replayed from a CUDA graph with L2 flushed before each."""
+    import torch
+    import torch.nn.functional as F
+
+    from tilegen_b200 import ops
+    from tilegen_b200.synthetic import DIT_SHAPES, dit_activations, gaussian_weight
+
+    rows = []
+    for name, k, n in DIT_SHAPES:
+        w = gaussian_weight(n, k, seed=1, dtype=torch.bfloat16, device=dev)
+        wq, ws = ops.rotate_quant(w, GROUP)
+        for m in (1, 4, 16, 64, 128):
+            x = dit_activations(name, m, seed=0, dtype=torch.float16, device=dev)
+            xb = x.to(torch.bfloat16)
+            kern = "gemv" if ops.gemv_route(m, n, k) else ("splitk" if ops.splitk_route(m, n, k) else "tiled")
+            t8 = _graph_us(lambda: ops.int8_gemm_dequant(*ops.rotate_quant(x, GROUP), wq, ws, None, torch.float16),
+                           flush)
+            tb = _graph_us(lambda: F.linear(xb, w), flush)
+            rows.append([name, m, kern, round(t8, 2), round(tb, 2), round(tb / t8, 3),
+                         round(n * k / (t8 * 1e-6) / 1e9 / hbm_gbs, 3)])
+        del w, wq, ws
+    return rows
+
+
 def _dit_block_bf16(dev, flush, stream, world, rank, tokens=65520, iters=10):
     """The DiT projection set on bf16 activations, `tokens` rows sharded over the ranks:
     per shape the max-over-ranks int8 linear and bf16 cuBLAS times and aggregate tokens/s."""
@@ -872,9 +951,11 @@ def run_tilegen(args):
     int8_lib_tops = _int_mm_tops(dev)
     status = _lib.device_status(local)
 
-    shapes = cpu = sweep = act_table = None
+    shapes = cpu = sweep = act_table = small_m = None
+    event_floor = _event_floor_us(dev, flush, stream)
     if world == 1:
         shapes = _shape_table(dev, flush, stream)
+        small_m = _small_m_table(dev, flush, peaks["hbm_gbs"])
         sweep = _quant_sweep(dev, flush, stream)
         act_table = _input_act_table(dev, flush, stream)
     # Last: seconds of sustained load that leave the GPU at its power cap.
@@ -924,7 +1005,9 @@ def run_tilegen(args):
         "quant_roofline": {"bound": "hbm", "kernel": "rotquant_kernel", "achieved": round(quant_gbs, 1),
                            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(quant_gbs / peaks["hbm_gbs"], 4),
                            "peak_source": peak_kind, "algorithmic_bytes_per_launch": quant_bytes,
-                           "traffic": QUANT_TRAFFIC_BYTES, "traffic_source": QUANT_TRAFFIC_SOURCE},
+                           "traffic": QUANT_TRAFFIC_BYTES, "traffic_source": QUANT_TRAFFIC_SOURCE,
+                           "timing": "one launch between two events after an L2 flush (quant_us)",
+                           "event_floor_us": round(event_floor, 2)},
         "e2e": {"value": round(e2e_plugin_us, 2), "unit": "us", "h2d_bytes_per_step": x.numel() * 2,
                 "d2h_bytes_per_step": m * n * 2,
                 "path": "one stream: pinned host x -> device, tilegen.comfyui.backend.int8_linear(convrot=True) "
@@ -948,10 +1031,21 @@ def run_tilegen(args):
         line["dit_shapes"] = shapes
     line["dit_block_bf16"] = {"tokens": 65520, "rows_sharded_over": world, "shapes": block}
     if sweep is not None:
+        for r in sweep:
+            if r[:4] == [GROUP, k, m, "fp16"] and r[7] is not None:
+                line["quant_roofline"]["back_to_back"] = {
+                    "us": r[7], "frac": r[8],
+                    "timing": "launches back to back over inputs that together exceed twice the L2 (quant_sweep "
+                              "us_stream)"}
         line["quant_sweep"] = {"columns": ["group", "K", "M", "dtype", "us", "GB/s", "frac_of_hbm", "us_stream",
                                            "frac_of_hbm_stream"], "rows": sweep}
     if gather is not None:
         line["gather_rows"] = gather
+    if small_m is not None:
+        line["small_m_linears"] = {"columns": ["shape", "M", "kernel", "int8_linear_us", "bf16_cublas_us",
+                                               "speedup_vs_bf16", "weight_stream_frac_of_hbm"], "rows": small_m,
+                                   "timing": "whole linears (rotate+quant + GEMM; bf16: F.linear) replayed 10 at a "
+                                             "time from a CUDA graph, L2 flushed before each, flush time subtracted"}
     if act_table is not None:
         line["input_act_ffn_down"] = act_table[0]
         line["rowwise_quant"] = {"columns": ["K", "M", "dtype", "us", "GB/s", "frac_of_hbm"], "rows": act_table[1]}

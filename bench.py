@@ -76,6 +76,13 @@ def _workload_desc():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
+    """SM clock and clock-event reasons during a with-block (the timed region).
+
+    A separate process reads NVML in a tight loop (wall-clock stamped), so the
+    samples do not depend on this process's interpreter lock, which the timed
+    loop holds while it enqueues; the samples stamped inside the with-block are
+    kept.  Falls back to ``nvidia-smi -lms 100`` when NVML is unavailable."""
+
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -84,6 +91,17 @@ class ClockSampler:
     NVML_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                     0x40: "hw_thermal_slowdown"}
 
+    POLL = ("import sys, time, pynvml\n"
+            "pynvml.nvmlInit()\n"
+            "h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))\n"
+            "print('max', pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)\n"
+            "while True:\n"
+            "    t = time.time()\n"
+            "    m = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)\n"
+            "    b = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)\n"
+            "    print(f'{t:.6f} {m} {b}', flush=True)\n"
+            "    time.sleep(0.0002)\n")
+
     def __init__(self, gpu_index: int):
         vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
         if 0 <= gpu_index < len(vis) and vis[gpu_index].strip().isdigit():
@@ -91,51 +109,45 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
-        self._nvml = None
-        self._thread = None
-        self._stop = False
-        self._samples = []  # (sm MHz, reason bits) read by NVML during the with-block
+        self.kind = None
+        self.t0 = self.t1 = 0.0
 
-    def _poll(self, nvml, handle):
-        while not self._stop:
-            try:
-                mhz = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
-                bits = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
-                self._samples.append((float(mhz), int(bits)))
-            except Exception:
-                return
-            time.sleep(0.0005)
+    def _lines(self):
+        try:
+            with open(self.path) as f:
+                return f.read().splitlines()
+        except OSError:
+            return []
 
     def __enter__(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        fd, self.path = tempfile.mkstemp(suffix=".txt")
         os.close(fd)
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-            time.sleep(0.3)
+            self.proc = subprocess.Popen([sys.executable, "-c", self.POLL, str(self.gpu)],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            self.kind = "nvml"
+            deadline = time.time() + 20
+            while len(self._lines()) < 2 and time.time() < deadline and self.proc.poll() is None:
+                time.sleep(0.01)
+            if len(self._lines()) < 2:
+                raise RuntimeError("NVML poller did not start")
         except Exception:
-            self.proc = None
-        # NVML read every ~0.5 ms while the with-block (the timed region, a few ms)
-        # runs: nvidia-smi's 100 ms period may not fall inside it at all.
-        try:
-            import threading
-
-            import pynvml
-
-            pynvml.nvmlInit()
-            handle = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
-            self._nvml = pynvml
-            self._thread = threading.Thread(target=self._poll, args=(pynvml, handle), daemon=True)
-            self._thread.start()
-        except Exception:
-            self._thread = None
+            if self.proc is not None:
+                self.proc.kill()
+            self.kind = "nvidia-smi"
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                time.sleep(0.3)
+            except Exception:
+                self.proc = None
+        self.t0 = time.time()
         return self
 
     def __exit__(self, *a):
-        self._stop = True
-        if self._thread is not None:
-            self._thread.join(5)
+        self.t1 = time.time()
+        time.sleep(0.005)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -144,23 +156,33 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        if self._samples:
-            smax = None
-            try:
-                h = self._nvml.nvmlDeviceGetHandleByIndex(self.gpu)
-                smax = float(self._nvml.nvmlDeviceGetMaxClockInfo(h, self._nvml.NVML_CLOCK_SM))
-            except Exception:
-                pass
-            reasons = sorted({nm for _, bits in self._samples for b, nm in self.NVML_REASONS.items() if bits & b})
-            if self.path and os.path.exists(self.path):
-                os.unlink(self.path)
-            return {"sm_mhz": statistics.median(m for m, _ in self._samples), "sm_max_mhz": smax,
-                    "samples": len(self._samples), "source": "NVML during the timed region", "reasons": reasons}
-        if not self.path or not os.path.exists(self.path):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        lines = self._lines()
+        if self.path and os.path.exists(self.path):
+            os.unlink(self.path)
+        if self.kind == "nvml":
+            smax, rows = None, []
+            for ln in lines:
+                parts = ln.split()
+                try:
+                    if parts[0] == "max":
+                        smax = float(parts[1])
+                    else:
+                        rows.append((float(parts[0]), float(parts[1]), int(parts[2])))
+                except (IndexError, ValueError):
+                    continue
+            inside = [r for r in rows if self.t0 <= r[0] <= self.t1]
+            used = inside or [r for r in rows if r[0] < self.t0][-1:] + [r for r in rows if r[0] > self.t1][:1]
+            if not used:
+                return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": ["unsampled"]}
+            reasons = sorted({nm for _, _, bits in used for b, nm in self.NVML_REASONS.items() if bits & b})
+            return {"sm_mhz": statistics.median(m for _, m, _ in used), "sm_max_mhz": smax,
+                    "samples": len(inside), "region_ms": round((self.t1 - self.t0) * 1e3, 2),
+                    "source": "NVML, polled by a separate process during the timed region"
+                              + ("" if inside else " (none inside: the samples just before and after)"),
+                    "reasons": reasons}
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
+        for line in lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -172,8 +194,9 @@ class ClockSampler:
             for nm, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
-        os.unlink(self.path)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "samples": len(sm),
                 "source": "nvidia-smi", "reasons": sorted(reasons)}
 
 

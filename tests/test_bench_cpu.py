@@ -55,3 +55,22 @@ def test_reference_cpu_path_is_the_installed_reference_when_present():
         assert os.path.realpath(quant.__code__.co_filename).startswith(
             os.path.realpath(os.path.join(bench.HERE, "baseline", "_ref")))
         assert quant.__module__ == "tilegen_ref.kernels.int8_convrot"
+
+
+def test_clock_sampler_keeps_samples_inside_the_region(tmp_path):
+    """NVML samples are stamped with wall-clock time; only those inside the
+    with-block count, and the reason bits map to the throttle names."""
+    c = bench.ClockSampler(0)
+    c.kind, c.path = "nvml", str(tmp_path / "clk.txt")
+    c.t0, c.t1 = 100.0, 100.010
+    (tmp_path / "clk.txt").write_text("max 1965\n99.9990 1965 0\n100.0010 1965 4\n100.0050 1950 4\n"
+                                      "100.0200 1300 8\n")
+    s = c.summary()
+    assert s["samples"] == 2 and s["sm_mhz"] == 1957.5 and s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap"]
+    c = bench.ClockSampler(0)
+    c.kind, c.path = "nvml", str(tmp_path / "clk2.txt")
+    c.t0, c.t1 = 100.0, 100.001
+    (tmp_path / "clk2.txt").write_text("max 1965\n99.9990 1965 0\n100.0020 1965 64\n")
+    s = c.summary()  # nothing inside: the samples just before and after
+    assert s["samples"] == 0 and s["reasons"] == ["hw_thermal_slowdown"]

@@ -24,6 +24,7 @@ def _worker(rank, world, port, m, q):
 
     import torch.distributed as dist
 
+    from tilegen_b200 import _lib
     from tilegen_b200.kernels.int8_convrot import quantize_convrot
     from tilegen_b200.quant import int8_matmul_dequant_chunked, quantize_convrot_weight
     from tilegen_b200.sharding import gather_rows, int8_convrot_linear_local, local_rows
@@ -38,10 +39,21 @@ def _worker(rank, world, port, m, q):
     try:
         x = outlier_activations(m, 5120, seed=0, dtype=torch.bfloat16).to(dev)
         wq, ws = quantize_convrot_weight(gaussian_weight(1024, 5120, seed=1, dtype=torch.bfloat16).to(dev), 256)
-        y = gather_rows(int8_convrot_linear_local(local_rows(x, world, rank), wq, ws, None, torch.bfloat16), m)
+        y_local = int8_convrot_linear_local(local_rows(x, world, rank), wq, ws, None, torch.bfloat16)
+        y = gather_rows(y_local, m)
         xq, xs = quantize_convrot(x, 256, backend="fht")
         ref = int8_matmul_dequant_chunked(xq, xs, wq, ws, None, torch.bfloat16)
-        q.put((rank, bool(torch.equal(y, ref)), tuple(y.shape)))
+        ok = bool(torch.equal(y, ref))
+        # In flight: the next layer runs on the SMs NCCL leaves (32 at 2 GPUs).
+        pending = gather_rows(y_local, m, async_op=True)
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        with pending.overlapped():
+            budget = int(_lib.lib().tg_sm_budget())
+            z = int8_convrot_linear_local(local_rows(x, world, rank), wq, ws, None, torch.bfloat16)
+        y2 = pending.wait()
+        ok = (ok and budget == sms - 32 and int(_lib.lib().tg_sm_budget()) == 0 and bool(torch.equal(y2, ref))
+              and bool(torch.equal(z, y_local)))
+        q.put((rank, ok, tuple(y.shape)))
     except Exception as e:  # report, never hang
         q.put((rank, False, f"{type(e).__name__}: {e}"[:200]))
     finally:
@@ -95,8 +107,11 @@ def _peer_worker(rank, world, port, m, q):
             xq, xs = quantize_convrot(local_rows(x, world, rank), 256, backend="fht")
             ops.int8_gemm_dequant(xq, xs, wq, ws, None, torch.bfloat16, out=g.local())
             pending = g.start()
-            other = other @ other.t() * 1e-4  # kernels in flight while the copy engines run
+            with pending.overlapped():  # kernels in flight while the copy engines run
+                other = other @ other.t() * 1e-4
+                nxt = quantize_convrot(local_rows(x, world, rank), 256, backend="fht")
             y = pending.wait()
+            ok = ok and bool(torch.equal(nxt[0], xq))
             xq, xs = quantize_convrot(x, 256, backend="fht")
             ref = int8_matmul_dequant_chunked(xq, xs, wq, ws, None, torch.bfloat16)
             ok = ok and bool(torch.equal(y, ref)) and tuple(y.shape) == (m, 1024)

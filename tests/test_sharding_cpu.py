@@ -55,7 +55,9 @@ def _worker(rank, world, port, m, fail_rank, q, overlap=False):
             # the gather in flight while the next layer runs on the local rows
             pending = gather_rows(y_local, m, async_op=True)
             w2 = torch.randint(-127, 128, (32, 256), dtype=torch.int8)
-            nxt = int8_convrot_linear_local(y_local.repeat(1, 4), w2, torch.rand(32) * 1e-2, None, torch.float32)
+            with pending.overlapped():  # gloo: nothing to reserve
+                nxt = int8_convrot_linear_local(y_local.repeat(1, 4), w2, torch.rand(32) * 1e-2, None,
+                                                torch.float32)
             y = pending.wait()
             ok = bool(torch.equal(y, ref)) and nxt.shape == (y_local.shape[0], 32) and pending.wait() is not None
         else:
@@ -103,3 +105,16 @@ def test_async_gather_overlaps_the_next_layer_gloo():
     res = _run(2, 33, overlap=True)
     assert [r[1] for r in res] == ["ok", "ok"], res
     assert all(r[2] for r in res) and all(r[3] == (33, 64) for r in res)
+
+
+def test_gather_sm_reserves():
+    """The SMs the next layer leaves to an in-flight gather (measured on B200)."""
+    from tilegen_b200 import sharding
+
+    assert sharding.nccl_gather_reserve(2) == 32 and sharding.nccl_gather_reserve(8) == 64
+    assert sharding.nccl_gather_reserve(4) == 64 and sharding.PEER_GATHER_RESERVE == 2
+    # A finished (or CPU) gather reserves nothing: the context is a no-op.
+    h = sharding.RowGather(None, torch.zeros(4, 2), None, 4, reserve=32)
+    with h.overlapped():
+        pass
+    assert torch.equal(h.wait(), torch.zeros(4, 2))

@@ -8,11 +8,17 @@ every rank, ``gather_rows`` all-gathers the blocks over NCCL (NVLink), as one
 collective outside the hot path; with ``async_op=True`` it returns at once and
 the caller overlaps the transfer with the next layer's kernels, waiting only
 where the gathered output is used.  The rotate+quant and GEMM kernels are
-persistent and size their grids for every SM, so run the next layer under
-``ops.sm_budget(sms - reserve)`` while a gather is in flight, leaving the
-collective's kernels the SMs they hold (NCCL 2.28's all-gather on B200: about
-32 SMs at 2 GPUs, 64 at 8; the copy-engine gather below: 2); otherwise part of
-the next layer's grid waits for the collective to finish.
+persistent and size their grids for every SM, so run the next layer inside the
+handle's ``overlapped()`` context (``ops.sm_budget(sms - reserve)``) while a
+gather is in flight, leaving the collective's kernels the SMs they hold (NCCL
+2.28's all-gather on B200: about 32 SMs at 2 GPUs, 64 at 8; the copy-engine
+gather below: 2); otherwise part of the next layer's grid waits for the
+collective to finish::
+
+    g = gather_rows(y_local, M, async_op=True)
+    with g.overlapped():
+        z_local = next_layer(x_local)
+    y = g.wait()
 
 Blocks are ``ceil(M / world)`` rows; the last rank's block may be short or
 empty.  ``gather_rows`` pads the short blocks to the common size for the
@@ -25,6 +31,7 @@ the transfer uses no SMs and the next layer's kernels keep all of them.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 
 import torch
@@ -46,16 +53,52 @@ def local_rows(x: torch.Tensor, world: int, rank: int) -> torch.Tensor:
     return x[s:e]
 
 
+def nccl_gather_reserve(world: int) -> int:
+    """SMs to leave to NCCL's all-gather while the next layer runs beside it.
+
+    Measured on B200 with NCCL 2.28 (65520 tokens, the next layer ffn_up): at 2
+    GPUs 32 (2442 -> 1933 us for gather + next layer), at 8 GPUs 64 (1367 ->
+    1045 us; 32 left there was slower than none).  Other sizes take the value of
+    the nearer measured one.
+    """
+    return 32 if world <= 2 else 64
+
+
+# SMs the copy-engine gather needs while the next layer runs: its one-element
+# all-reduce (the ready signal) must find one.
+PEER_GATHER_RESERVE = 2
+
+
+@contextlib.contextmanager
+def _reserve_sms(device: torch.device, reserve: int):
+    from . import ops
+
+    if device.type != "cuda" or reserve <= 0:
+        yield
+        return
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    with ops.sm_budget(max(1, sms - reserve)):
+        yield
+
+
 class RowGather:
     """An all-gather of row blocks in flight (``gather_rows(..., async_op=True)``).
 
     ``wait()`` returns the gathered ``[m_total, N]`` tensor.  On NCCL it only
     makes the caller's current stream wait for the collective (the host does not
-    block), so kernels enqueued before ``wait()`` overlap the transfer.
+    block), so kernels enqueued before ``wait()`` overlap the transfer; enqueue
+    them inside ``with handle.overlapped():``, which sizes the persistent kernels'
+    grids for the SMs the collective leaves (``nccl_gather_reserve``).
     """
 
-    def __init__(self, work, out: torch.Tensor, parts: list | None, m_total: int):
+    def __init__(self, work, out: torch.Tensor, parts: list | None, m_total: int, reserve: int = 0):
         self._work, self._out, self._parts, self._m = work, out, parts, m_total
+        self.reserve = reserve
+
+    def overlapped(self):
+        """Context for the kernels that run while this gather is in flight."""
+        dev = self._out.device if self._out is not None else torch.device("cpu")
+        return _reserve_sms(dev, self.reserve if self._work is not None else 0)
 
     def wait(self) -> torch.Tensor:
         if self._work is not None:
@@ -88,7 +131,8 @@ def gather_rows(y_local: torch.Tensor, m_total: int, group=None, async_op: bool 
         parts = [torch.empty_like(buf) for _ in range(world)]
         work = dist.all_gather(parts, buf, group=group, async_op=async_op)
         out = None if async_op else torch.cat(parts, 0)
-    handle = RowGather(work if async_op else None, out, parts if async_op else None, m_total)
+    reserve = nccl_gather_reserve(world) if out is not None else 0
+    handle = RowGather(work if async_op else None, out, parts if async_op else None, m_total, reserve)
     return handle if async_op else handle.wait()
 
 
@@ -105,10 +149,16 @@ _INT_VIEW = {1: (torch.int8, "|i1"), 2: (torch.int16, "<i2"), 4: (torch.int32, "
 
 class PeerGather:
     """A ``PeerRowGather.start()`` in flight; ``wait()`` orders the caller's current
-    stream after the copies and returns the gathered ``[m_total, N]`` tensor."""
+    stream after the copies and returns the gathered ``[m_total, N]`` tensor.
+    Enqueue the kernels that overlap it inside ``with handle.overlapped():``."""
 
     def __init__(self, events: list, out: torch.Tensor):
         self._events, self._out = events, out
+        self.reserve = PEER_GATHER_RESERVE
+
+    def overlapped(self):
+        """Context for the kernels that run while these copies are in flight."""
+        return _reserve_sms(self._out.device, self.reserve if self._events else 0)
 
     def wait(self) -> torch.Tensor:
         cur = torch.cuda.current_stream(self._out.device)
@@ -132,8 +182,9 @@ class PeerRowGather:
        several copy engines run at once; nothing waits on the host;
     3. ``wait()`` on the returned handle (the caller's current stream waits for the
        copies) gives the full output.  Kernels enqueued between ``start()`` and
-       ``wait()`` overlap the transfer; run them under ``ops.sm_budget(sms - 2)``
-       so that the one-element all-reduce finds an SM.
+       ``wait()`` overlap the transfer; enqueue them inside the handle's
+       ``overlapped()`` context (``ops.sm_budget(sms - 2)``) so that the
+       one-element all-reduce finds an SM.
 
     The two buffers alternate between steps, so a step's rows may be written while
     peers may still copy the previous step's.  Call ``wait()`` on one step's gather

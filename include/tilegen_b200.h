@@ -103,6 +103,29 @@ int tg_quantize_act(const void *x, int x_dtype, int64_t M, int64_t K, int group,
                     void *stream);
 
 /*
+ * The rotated quantiser with the DiT block's normalisation in front of it, in
+ * the same pass over x: for row m and v = m / mod_rows,
+ *   y[m,:] = LayerNorm(x[m,:]) * (1 + mod_scale[v,:]) + mod_shift[v,:]
+ * (LayerNorm without affine, epsilon `eps`), then tg_rotate_quant on y.  The
+ * normalised row, the product and the sum are each rounded to x_dtype, as the
+ * separate torch ops would store them; the row mean and variance are fp32 sums
+ * in a fixed order, rstd = 1 / sqrt(var + eps).  The reference's path starts at
+ * int8_linear's input, so this has no reference counterpart: it removes the
+ * write and re-read of the modulated activations between the block's
+ * normalisation and its projection.
+ *
+ *   x                   [M, K] fp16/bf16, 16-B aligned; K % 256 == 0
+ *   group               4, 16, 64 or 256 (rotated; the short butterfly order)
+ *   mod_scale/mod_shift [ceil(M / mod_rows), K] of x_dtype, 16-B aligned
+ *   mod_rows            rows per modulation vector (>= 1; M for one vector)
+ *   q, scale            as tg_rotate_quant
+ * TG_ERR_INVALID_ARG for eps < 0, NaN or inf, mod_rows < 1; M == 0 is a no-op.
+ */
+int tg_quantize_ln_mod(const void *x, int x_dtype, int64_t M, int64_t K, int group, float eps,
+                       const void *mod_scale, const void *mod_shift, int64_t mod_rows, int8_t *q, float *scale,
+                       void *stream);
+
+/*
  * INT8 GEMM with the dequantisation fused into the epilogue (tcgen05 kind::i8,
  * int32 accumulators in tensor memory).
  *

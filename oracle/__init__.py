@@ -53,6 +53,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_int8_gemm_dequant.restype = ctypes.c_int
         L.oracle_num_threads.restype = ctypes.c_int
         L.oracle_set_num_threads.argtypes = [ctypes.c_int]
+        L.oracle_ln_mod.argtypes = [p, ctypes.c_int, i64, i64, ctypes.c_float, p, p, i64, p]
+        L.oracle_ln_mod.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -81,6 +83,24 @@ def rotate_quant(x: np.ndarray, dtype: str, group: int = 256, order: str = "refe
     if rc != 0:
         raise ValueError(f"oracle_rotate_quant rejected M={m} K={k} group={group}")
     return q, s
+
+
+def ln_mod(x: np.ndarray, dtype: str, eps: float, scale: np.ndarray, shift: np.ndarray, mod_rows: int):
+    """``LayerNorm(x) * (1 + scale[v]) + shift[v]`` per row (``v = row // mod_rows``) in
+    the CUDA prologue's arithmetic; all arrays hold raw fp16/bf16 patterns.  Returns
+    the ``[M, K]`` patterns of the modulated rows."""
+    x = np.ascontiguousarray(x).view(np.uint16)
+    scale = np.ascontiguousarray(scale).view(np.uint16)
+    shift = np.ascontiguousarray(shift).view(np.uint16)
+    m, k = x.shape
+    if scale.shape != shift.shape or scale.shape[1] != k or scale.shape[0] < -(-m // mod_rows):
+        raise ValueError("modulation vectors must be [ceil(M / mod_rows), K]")
+    y = np.empty((m, k), np.uint16)
+    rc = lib().oracle_ln_mod(_ptr(x), _DTYPE_CODES[dtype], m, k, float(eps), _ptr(scale), _ptr(shift),
+                             int(mod_rows), _ptr(y))
+    if rc != 0:
+        raise ValueError(f"oracle_ln_mod rejected M={m} K={k} dtype={dtype}")
+    return y
 
 
 def rowwise_quant(x: np.ndarray, dtype: str):

@@ -33,6 +33,11 @@
  *      dtype, round half to even, clamp to [-128, 127] (NaN kept), int8 cast
  *      (NaN -> 0).
  *
+ *  oracle_ln_mod - the DiT block's LayerNorm (no affine) and modulation in front
+ *      of a projection, y = LN(x) * (1 + scale) + shift, as the CUDA kernel's
+ *      fused prologue evaluates it (no reference counterpart: the reference's
+ *      path starts at int8_linear's input).  Defined where it is.
+ *
  * Build with -ffp-contract=off: a contracted a*b+c would change the rounding.
  */
 #include <math.h>
@@ -262,6 +267,78 @@ int oracle_rotate_quant_short(const void *x, int dtype, int64_t M, int64_t K, in
 
 static float round_to_dtype(float v, int dtype) {
     return dtype == DT_BF16 ? bf16_to_f32(f32_to_bf16(v)) : f16_to_f32(f32_to_f16(v));
+}
+
+/* Sum of one row's per-line partials part[0..lines) in the kernel's fixed
+ * order: column c < 16 adds lines c, c + 16, c + 32, ... ascending, then the
+ * column sums are added in ascending order. */
+static float ln_row_total(const float *part, int lines) {
+    const int cols = lines < 16 ? lines : 16;
+    float tot = 0.0f;
+    for (int c = 0; c < cols; ++c) {
+        float t = part[c];
+        for (int l = c + 16; l < lines; l += 16) t += part[l];
+        tot = c == 0 ? t : tot + t;
+    }
+    return tot;
+}
+
+/* y = dtype(dtype(dtype((x - mean) * rstd) * dtype(1 + scale[v])) + shift[v])
+ * for row m and v = m / mod_rows, with, per row of K = 64 * lines values:
+ *   line sums: pairs (2k, 2k+1) of the line's 64 values accumulated in two
+ *     lanes, k ascending, then lane 0 + lane 1; mean = total(line sums) / K;
+ *   d = x - mean; line sums of squares the same way with fmaf(d, d, acc);
+ *   var = total / K; rstd = 1 / sqrtf(var + eps);
+ * every operation in fp32 rounded once, then each named rounding to the dtype.
+ * x, scale, shift, y hold raw fp16/bf16 patterns ([M][K], [.][K], [.][K], [M][K]).
+ * Returns 0 on success, -1 on a bad argument. */
+int oracle_ln_mod(const uint16_t *x, int dtype, int64_t M, int64_t K, float eps, const uint16_t *scale,
+                  const uint16_t *shift, int64_t mod_rows, uint16_t *y) {
+    if ((dtype != DT_F16 && dtype != DT_BF16) || K <= 0 || K % 64 != 0 || K / 64 > 1024 || M < 0 ||
+        mod_rows < 1)
+        return -1;
+    const int lines = (int)(K / 64);
+#pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m) {
+        float part[1024];
+        float d[64];
+        const int64_t v = m / mod_rows;
+        for (int l = 0; l < lines; ++l) {
+            float a0 = 0.0f, a1 = 0.0f;
+            for (int k = 0; k < 32; ++k) {
+                const float e0 = load_elem(x, dtype, m * K + l * 64 + 2 * k);
+                const float e1 = load_elem(x, dtype, m * K + l * 64 + 2 * k + 1);
+                a0 = k == 0 ? e0 : a0 + e0;
+                a1 = k == 0 ? e1 : a1 + e1;
+            }
+            part[l] = a0 + a1;
+        }
+        const float mean = ln_row_total(part, lines) / (float)K;
+        for (int l = 0; l < lines; ++l) {
+            float q0 = 0.0f, q1 = 0.0f;
+            for (int k = 0; k < 32; ++k) {
+                const float d0 = load_elem(x, dtype, m * K + l * 64 + 2 * k) - mean;
+                const float d1 = load_elem(x, dtype, m * K + l * 64 + 2 * k + 1) - mean;
+                q0 = fmaf(d0, d0, q0);
+                q1 = fmaf(d1, d1, q1);
+            }
+            part[l] = q0 + q1;
+        }
+        const float var = ln_row_total(part, lines) / (float)K;
+        const float rstd = 1.0f / sqrtf(var + eps);
+        for (int l = 0; l < lines; ++l) {
+            for (int j = 0; j < 64; ++j) d[j] = load_elem(x, dtype, m * K + l * 64 + j) - mean;
+            for (int j = 0; j < 64; ++j) {
+                const int64_t c = (int64_t)l * 64 + j;
+                const float xn = round_to_dtype(d[j] * rstd, dtype);
+                const float t1 = round_to_dtype(1.0f + load_elem(scale, dtype, v * K + c), dtype);
+                const float pr = round_to_dtype(xn * t1, dtype);
+                const float out = pr + load_elem(shift, dtype, v * K + c);
+                y[m * K + c] = dtype == DT_BF16 ? f32_to_bf16(out) : f32_to_f16(out);
+            }
+        }
+    }
+    return 0;
 }
 
 /* Returns 0 on success, -1 on a bad argument (dtype must be DT_F16 or DT_BF16). */

@@ -118,6 +118,26 @@ def test_gemv_entry_points_check_before_device_work():
     assert L.tg_int8_gemv_dequant_config(64, 64, None, None) == _lib.TG_ERR_INVALID_ARG
 
 
+def test_ln_mod_entry_checks_before_device_work():
+    L = _lib.lib()
+    p = ctypes.c_void_p(256)
+    f16 = _lib.TG_DT_F16
+    assert "tg_quantize_ln_mod" in _lib.declared_functions()
+    # eps negative or NaN, mod_rows < 1, fp32 input, the row-wise group, K not a multiple of 256
+    assert L.tg_quantize_ln_mod(p, f16, 4, 512, 256, -1.0, p, p, 1, p, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_quantize_ln_mod(p, f16, 4, 512, 256, float("nan"), p, p, 1, p, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_quantize_ln_mod(p, f16, 4, 512, 256, 1e-6, p, p, 0, p, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_quantize_ln_mod(p, _lib.TG_DT_F32, 4, 512, 256, 1e-6, p, p, 1, p, p, None) == \
+        _lib.TG_ERR_INVALID_ARG
+    assert L.tg_quantize_ln_mod(p, f16, 4, 512, 1, 1e-6, p, p, 1, p, p, None) == _lib.TG_ERR_UNSUPPORTED
+    assert L.tg_quantize_ln_mod(p, f16, 4, 320, 64, 1e-6, p, p, 1, p, p, None) == _lib.TG_ERR_UNSUPPORTED
+    # missing or misaligned modulation vectors; M == 0 is a no-op
+    assert L.tg_quantize_ln_mod(p, f16, 4, 512, 256, 1e-6, None, p, 1, p, p, None) == _lib.TG_ERR_INVALID_ARG
+    assert L.tg_quantize_ln_mod(p, f16, 4, 512, 256, 1e-6, p, ctypes.c_void_p(258), 1, p, p, None) == \
+        _lib.TG_ERR_MISALIGNED
+    assert L.tg_quantize_ln_mod(None, f16, 0, 512, 256, 1e-6, None, None, 1, None, None, None) == _lib.TG_OK
+
+
 def test_quantize_act_checks_before_device_work():
     L = _lib.lib()
     p = ctypes.c_void_p(16)

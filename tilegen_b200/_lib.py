@@ -102,6 +102,8 @@ def lib() -> ctypes.CDLL:
         L.tg_rotate_quant_max_k.restype = i64
         L.tg_quantize_act.argtypes = [p, i32, i64, i64, i32, i32, p, p, p]
         L.tg_quantize_act.restype = i32
+        L.tg_quantize_ln_mod.argtypes = [p, i32, i64, i64, i32, ctypes.c_float, p, p, i64, p, p, p]
+        L.tg_quantize_ln_mod.restype = i32
         L.tg_int8_gemm_dequant.argtypes = [p, p, p, p, i64, p, i32, i64, i64, i64, i32, p, p]
         L.tg_int8_gemm_dequant.restype = i32
         L.tg_gemm_config.argtypes = [i64, i64, ctypes.POINTER(i32), ctypes.POINTER(i32)]

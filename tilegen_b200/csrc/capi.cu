@@ -85,9 +85,11 @@ bool ensure_smem_attr(K kernel, int dev, uint32_t bytes, uint32_t* done_bytes) {
 
 // ------------------------------------------------------------------ rotate+quant
 // Dynamic shared memory of a launch: alignment slack, the ring of `stages`
-// slots, their mbarriers, and the row maxima and NaN flags ([3][R] each).
-uint32_t rotquant_smem(int stages, uint32_t stage_bytes, int R) {
-  return 1024u + uint32_t(stages) * stage_bytes + uint32_t(stages) * 8u + uint32_t(6 * R) * 4u;
+// slots, their mbarriers, the row maxima and NaN flags ([3][R] each), and for
+// the LayerNorm prologue its partial sums (the CTA has stage_bytes / 128 threads).
+uint32_t rotquant_smem(int stages, uint32_t stage_bytes, int R, bool ln) {
+  const uint32_t ln_bytes = ln ? uint32_t(tg::ln_words(int(stage_bytes / 128u), R)) * 4u : 0u;
+  return 1024u + uint32_t(stages) * stage_bytes + uint32_t(stages) * 8u + uint32_t(6 * R) * 4u + ln_bytes;
 }
 
 constexpr uint32_t kSmemPerCtaMax = 232448u;  // 227 KB: the opt-in maximum of one CTA
@@ -116,13 +118,15 @@ bool rotquant_shape(int dev, int threads, uint32_t stage_bytes, int R, int* occ_
   const uint32_t dyn_max = kSmemPerCtaMax - static_smem;  // static + dynamic <= the per-CTA maximum
   if (!ensure_smem_attr(kern, dev, dyn_max, attr_done)) return false;
   int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, rotquant_smem(2, stage_bytes, R)) !=
+  constexpr bool kLn = ACT == tg::kActLnMod;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, rotquant_smem(2, stage_bytes, R, kLn)) !=
           cudaSuccess ||
       occ < 1)
     return false;
   int stages = 4;
-  while (stages > 2 && (rotquant_smem(stages, stage_bytes, R) > dyn_max ||
-                        uint64_t(occ) * (rotquant_smem(stages, stage_bytes, R) + static_smem + 1024u) > kSmemPerSm))
+  while (stages > 2 && (rotquant_smem(stages, stage_bytes, R, kLn) > dyn_max ||
+                        uint64_t(occ) * (rotquant_smem(stages, stage_bytes, R, kLn) + static_smem + 1024u) >
+                            kSmemPerSm))
     --stages;
   *occ_out = occ;
   *stages_out = stages;
@@ -134,7 +138,7 @@ template <int NST, bool BF16, int ACT, bool EXACT, int REGS>
 int launch_rotquant_t(const CUtensorMap& tm, tg::RotQuantParams p, int threads, int occ, int dev, int sms,
                       cudaStream_t st) {
   auto kern = tg::rotquant_kernel<NST, BF16, ACT, EXACT, REGS>;
-  const uint32_t smem = rotquant_smem(p.stages, p.stage_bytes, p.rows_per_batch);
+  const uint32_t smem = rotquant_smem(p.stages, p.stage_bytes, p.rows_per_batch, ACT == tg::kActLnMod);
   const int64_t grid64 = std::min<int64_t>(p.nbatches, int64_t(sms) * occ);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -175,6 +179,10 @@ int launch_rotquant_regs(const CUtensorMap& tm, tg::RotQuantParams p, int thread
   return launch_rotquant_t<NST, BF16, ACT, EXACT, 96>(tm, p, threads, occ, dev, sms, st);
 }
 
+// Internal code of the LayerNorm + modulation prologue (tg_quantize_ln_mod),
+// beside the public TG_ACT_* codes.
+constexpr int kLnModCode = 3;
+
 template <int NST, bool BF16, bool EXACT>
 int launch_rotquant_act(int act, const CUtensorMap& tm, const tg::RotQuantParams& p, int threads, int dev, int sms,
                         cudaStream_t st) {
@@ -182,6 +190,13 @@ int launch_rotquant_act(int act, const CUtensorMap& tm, const tg::RotQuantParams
     case TG_ACT_GELU_TANH:
       return launch_rotquant_regs<NST, BF16, tg::kActGeluTanh, EXACT>(tm, p, threads, dev, sms, st);
     case TG_ACT_GELU: return launch_rotquant_regs<NST, BF16, tg::kActGelu, EXACT>(tm, p, threads, dev, sms, st);
+    case kLnModCode:
+      // Built for the rotated groups in the short order only.
+      if constexpr (NST > 0 && !EXACT) {
+        return launch_rotquant_regs<NST, BF16, tg::kActLnMod, EXACT>(tm, p, threads, dev, sms, st);
+      } else {
+        return TG_ERR_UNSUPPORTED;
+      }
     default: return launch_rotquant_regs<NST, BF16, tg::kActNone, EXACT>(tm, p, threads, dev, sms, st);
   }
 }
@@ -207,6 +222,19 @@ int gcd_int(int a, int b) {
   }
   return a;
 }
+
+// The LayerNorm + modulation prologue's arguments (tg_quantize_ln_mod).
+struct LnModArgs {
+  const void* scale;
+  const void* shift;
+  int64_t rows;
+  float eps;
+};
+
+// The shared body of tg_quantize_act and tg_quantize_ln_mod: shape checks,
+// launch shape, tensor map, launch.
+int quantize_launch(const void* x, int x_dtype, int64_t M, int64_t K, int group, int act, bool exact,
+                    const LnModArgs* ln, int8_t* q, float* scale, void* stream);
 
 }  // namespace
 
@@ -244,6 +272,29 @@ int tg_quantize_act(const void* x, int x_dtype, int64_t M, int64_t K, int group,
   const bool exact = (act & TG_QUANT_REFERENCE_ORDER) != 0;
   act &= ~TG_QUANT_REFERENCE_ORDER;
   if (act != TG_ACT_NONE && act != TG_ACT_GELU_TANH && act != TG_ACT_GELU) return TG_ERR_INVALID_ARG;
+  return quantize_launch(x, x_dtype, M, K, group, act, exact, nullptr, q, scale, stream);
+}
+
+int tg_quantize_ln_mod(const void* x, int x_dtype, int64_t M, int64_t K, int group, float eps, const void* mod_scale,
+                       const void* mod_shift, int64_t mod_rows, int8_t* q, float* scale, void* stream) {
+  if (M < 0 || K <= 0 || mod_rows < 1) return TG_ERR_INVALID_ARG;
+  if (x_dtype != TG_DT_F16 && x_dtype != TG_DT_BF16) return TG_ERR_INVALID_ARG;
+  if (!(eps >= 0.0f) || eps > 3.0e38f) return TG_ERR_INVALID_ARG;  // also rejects NaN
+  if (group == 1) return TG_ERR_UNSUPPORTED;                         // rotated groups only
+  if (M > 0) {
+    if (!mod_scale || !mod_shift) return TG_ERR_INVALID_ARG;
+    if (!aligned16(mod_scale) || !aligned16(mod_shift)) return TG_ERR_MISALIGNED;
+  }
+  const LnModArgs ln{mod_scale, mod_shift, mod_rows, eps};
+  return quantize_launch(x, x_dtype, M, K, group, kLnModCode, false, &ln, q, scale, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+int quantize_launch(const void* x, int x_dtype, int64_t M, int64_t K, int group, int act, bool exact,
+                    const LnModArgs* ln, int8_t* q, float* scale, void* stream) {
   int nst;
   switch (group) {
     case 1: nst = 0; break;
@@ -313,6 +364,10 @@ int tg_quantize_act(const void* x, int x_dtype, int64_t M, int64_t K, int group,
   p.stages = 2;
   p.stage_bytes = stage_bytes;
   p.seg = gcd_int(cpr, 32);
+  p.mod_scale = ln ? ln->scale : nullptr;
+  p.mod_shift = ln ? ln->shift : nullptr;
+  p.mod_rows = ln ? ln->rows : 1;
+  p.ln_eps = ln ? ln->eps : 0.0f;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf = x_dtype == TG_DT_BF16;
@@ -332,7 +387,7 @@ int tg_quantize_act(const void* x, int x_dtype, int64_t M, int64_t K, int group,
 #undef TG_RQ_CASE
 }
 
-}  // extern "C"
+}  // namespace
 
 namespace {
 

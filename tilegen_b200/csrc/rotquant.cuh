@@ -59,7 +59,63 @@ struct RotQuantParams {
   int stages;            // shared-memory ring depth
   uint32_t stage_bytes;  // bytes per ring slot = blockDim.x * 128 (a multiple of 1024)
   int seg;               // lanes per absmax shuffle segment = gcd(cpr, 32)
+  // kActLnMod only: modulation vectors [ceil(M / mod_rows), K] of x's dtype
+  // (rows r use vector r / mod_rows) and the LayerNorm epsilon.
+  const void* mod_scale;
+  const void* mod_shift;
+  int64_t mod_rows;
+  float ln_eps;
 };
+
+// Words of shared memory the LayerNorm prologue needs beyond the ring, the
+// barriers and the row maxima: per-line partial sums of x and of (x - mean)^2
+// ([R][lines]) and their 16 column sums ([R][16]), for a CTA of `threads`
+// threads (lines <= threads / R).
+__host__ __device__ constexpr int ln_words(int threads, int R) { return 2 * threads + 2 * 16 * R; }
+
+// Packed round-to-nearest add and multiply of two x-dtype pairs held as the
+// bits of 32-bit words.
+template <bool BF16>
+__device__ __forceinline__ uint32_t hadd2_dt(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if (BF16) asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t hmul2_dt(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if (BF16) asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  // Opaque to the compiler: the product is rounded on its own, never
+  // contracted with the add that follows into one fma.
+  asm volatile("" : "+r"(r));
+  return r;
+}
+
+// Sum of one row's per-line partials in a fixed order: column c < 16 of the
+// row adds lines c, c + 16, c + 32, ... (ascending), then every thread adds the
+// (up to) 16 column sums in ascending order.  Two CTA barriers; every thread of
+// the CTA must call it.  `part` [R][lines], `col` [R][16].
+__device__ __forceinline__ float row_total(float* part, float* col, float mine, bool active, int row_local,
+                                           int chunk, int cpr) {
+  if (active) part[row_local * cpr + chunk] = mine;
+  __syncthreads();
+  const int cols = cpr < 16 ? cpr : 16;
+  if (active && chunk < cols) {
+    float t = part[row_local * cpr + chunk];
+    for (int c = chunk + 16; c < cpr; c += 16) t = __fadd_rn(t, part[row_local * cpr + c]);
+    col[row_local * 16 + chunk] = t;
+  }
+  __syncthreads();
+  float tot = 0.0f;
+  if (active) {
+    tot = col[row_local * 16];
+    for (int c = 1; c < cols; ++c) tot = __fadd_rn(tot, col[row_local * 16 + c]);
+  }
+  return tot;
+}
 
 // One radix-4 butterfly, each output evaluated exactly as
 //   y0 = a0 + a1 + a2 - a3, y1 = a0 + a1 - a2 + a3,
@@ -175,8 +231,10 @@ __device__ __forceinline__ void stage2_64(float2 (&vp)[32]) {
   for (int l = 0; l < 8; ++l) bfly4x2(vp[l], vp[l + 8], vp[l + 16], vp[l + 24]);
 }
 
-// Input activations (the names of backend.py's `input_act`).
-enum : int { kActNone = 0, kActGeluTanh = 1, kActGelu = 2 };
+// Input operations applied to x before the rotation: the activations (the
+// names of backend.py's `input_act`), and kActLnMod, the DiT block's
+// LayerNorm (no affine) followed by its modulation, y = LN(x) * (1 + scale) + shift.
+enum : int { kActNone = 0, kActGeluTanh = 1, kActGelu = 2, kActLnMod = 3 };
 
 // The activation in fp32 on a pair, written as torch's CUDA GELU kernels
 // evaluate it in their fp32 op-math -- the same operations in the same order
@@ -234,7 +292,7 @@ __device__ __forceinline__ void unpack8(const uint4 w, float2* f) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     f[i] = unpack2_dtype<BF16>(u[i]);
-    if (ACT != kActNone) f[i] = unpack2_dtype<BF16>(pack2_dtype<BF16>(act2_f32<ACT>(f[i])));
+    if (ACT == kActGeluTanh || ACT == kActGelu) f[i] = unpack2_dtype<BF16>(pack2_dtype<BF16>(act2_f32<ACT>(f[i])));
   }
 }
 
@@ -412,6 +470,7 @@ __global__ void __maxnreg__(REGS) rotquant_kernel(const __grid_constant__ CUtens
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(stages) * stage_bytes);
   unsigned* rowmax = reinterpret_cast<unsigned*>(full + stages);  // [3][R] maxima, then [3][R] NaN flags
+  float* const ln_area = reinterpret_cast<float*>(rowmax + 6 * R);  // kActLnMod: ln_words(blockDim.x, R)
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x;
@@ -494,6 +553,58 @@ __global__ void __maxnreg__(REGS) rotquant_kernel(const __grid_constant__ CUtens
       for (int c = 0; c < 8; ++c) {
         const uint4 w = *reinterpret_cast<const uint4*>(buf + (line_off ^ uint32_t(c << 4)));
         unpack8<BF16, ACT>(w, &vp[4 * c]);
+      }
+    }
+    if constexpr (ACT == kActLnMod) {
+      // LayerNorm over the row (no affine), then the modulation, each result in
+      // x's dtype as the separate ops would store it: mean and variance in fp32
+      // summed in a fixed order (per line over its 64 values in pairs, then
+      // row_total), rstd = 1 / sqrt(var + eps), xn = dtype((x - mean) * rstd),
+      // y = dtype(dtype(xn * dtype(1 + scale)) + shift).  The last three are
+      // packed half-precision adds and multiplies: each gives the fp32 result
+      // rounded to the dtype, because 24 bits hold the exact product of two
+      // 11-bit (or 8-bit) significands and rounding an fp32 sum or product
+      // again to a format of at most 11 bits is innocuous (24 >= 2 * 11 + 2).
+      float* const part_s = ln_area;
+      float* const col_s = part_s + blockDim.x;
+      float* const part_q = col_s + 16 * R;
+      float* const col_q = part_q + blockDim.x;
+      float2 a = vp[0];
+#pragma unroll
+      for (int k = 1; k < 32; ++k) a = add2(a, vp[k]);
+      const float mean =
+          __fdiv_rn(row_total(part_s, col_s, __fadd_rn(a.x, a.y), active, row_local, chunk, cpr), float(K));
+      const float2 neg_mean = make_float2(-mean, -mean);
+      float2 sq = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        vp[k] = add2(vp[k], neg_mean);
+        sq = fma2(vp[k], vp[k], sq);
+      }
+      const float var =
+          __fdiv_rn(row_total(part_q, col_q, __fadd_rn(sq.x, sq.y), active, row_local, chunk, cpr), float(K));
+      const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.ln_eps)));
+      const float2 rstd2 = make_float2(rstd, rstd);
+      // Modulation vector of this row (rows past M, which are never stored,
+      // read the last row's).
+      const int64_t row64 = int64_t(batch) * R + row_local;
+      const int64_t vec = (row64 < p.M ? row64 : p.M - 1) / p.mod_rows;
+      const size_t voff = size_t(vec) * size_t(K) + size_t(chunk) * 64u;
+      const uint4* scv = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.mod_scale) + voff);
+      const uint4* shv = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.mod_shift) + voff);
+      const uint32_t one2 = BF16 ? 0x3f803f80u : 0x3c003c00u;  // (1, 1) in the dtype
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 sw = active ? __ldg(scv + c) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 hw = active ? __ldg(shv + c) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t su[4] = {sw.x, sw.y, sw.z, sw.w};
+        const uint32_t hu[4] = {hw.x, hw.y, hw.z, hw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t xn = pack2_dtype<BF16>(mul2(vp[4 * c + i], rstd2));
+          const uint32_t y = hadd2_dt<BF16>(hmul2_dt<BF16>(xn, hadd2_dt<BF16>(one2, su[i])), hu[i]);
+          vp[4 * c + i] = unpack2_dtype<BF16>(y);
+        }
       }
     }
     if (EXACT) {

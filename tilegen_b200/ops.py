@@ -135,6 +135,59 @@ def quantize_act(x: torch.Tensor, group: int = 256, act: str | None = None, orde
     return q, s
 
 
+def quantize_ln_mod(x: torch.Tensor, group: int, scale: torch.Tensor, shift: torch.Tensor, eps: float = 1e-6,
+                    rows_per_vector: int | None = None):
+    """The DiT block's normalisation in front of a projection, fused into the
+    quantiser (``tg_quantize_ln_mod``): ``y = LayerNorm(x) * (1 + scale) + shift``
+    (LayerNorm without affine, ``eps``), then rotate+quantise ``y`` with ``group``
+    (4..256, the short butterfly order), in one pass over ``x`` -- the modulated
+    activations are never written to memory.
+
+    ``x``: ``[..., K]`` fp16/bf16 CUDA, flattened to ``[M, K]`` rows.  ``scale`` and
+    ``shift``: ``[K]`` (one vector) or ``[S, ..., K]`` (``S`` vectors, e.g. a DiT's
+    per-sample ``[B, 1, K]``), converted to ``x``'s dtype; row ``r`` uses vector
+    ``r // rows_per_vector`` (default ``M // S``, which must divide evenly).  Each
+    of the normalised row, the product and the sum is rounded to ``x``'s dtype as
+    torch's separate ops store them; the mean and variance are fp32 sums in a
+    fixed order, so codes match ``F.layer_norm`` + the two ops + ``rotate_quant``
+    within the parity tolerance, not bit for bit.  Returns ``(q int8 [M, K],
+    scale fp32 [M])``.
+    """
+    if not isinstance(x, torch.Tensor) or not x.is_cuda:
+        raise ValueError("quantize_ln_mod: CUDA tensor required")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"quantize_ln_mod: fp16/bf16 input required, got {x.dtype}")
+    if group not in _SUPPORTED_GROUPS:
+        raise ValueError(f"quantize_ln_mod: group must be one of {_SUPPORTED_GROUPS}, got {group}")
+    k = x.shape[-1]
+    if k % 256:
+        raise ValueError(f"quantize_ln_mod: K={k} must be a multiple of 256")
+    x2 = _aligned(x.reshape(-1, k))
+    m = x2.shape[0]
+    vecs = []
+    for name, t in (("scale", scale), ("shift", shift)):
+        if not isinstance(t, torch.Tensor) or t.shape[-1] != k:
+            raise ValueError(f"quantize_ln_mod: {name} must be a tensor whose last dimension is K={k}")
+        vecs.append(_aligned(t.to(device=x.device, dtype=x.dtype).reshape(-1, k)))
+    sc, sh = vecs
+    if sc.shape != sh.shape:
+        raise ValueError(f"quantize_ln_mod: scale {tuple(scale.shape)} and shift {tuple(shift.shape)} differ")
+    nvec = sc.shape[0]
+    if rows_per_vector is None:
+        if m % nvec:
+            raise ValueError(f"quantize_ln_mod: {m} rows do not split evenly over {nvec} modulation vectors")
+        rows_per_vector = max(1, m // nvec)
+    rows_per_vector = int(rows_per_vector)
+    if rows_per_vector < 1 or nvec < -(-m // rows_per_vector):
+        raise ValueError(f"quantize_ln_mod: {nvec} vectors cannot cover {m} rows at {rows_per_vector} a vector")
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m,), dtype=torch.float32, device=x.device)
+    if m:
+        _call("tg_quantize_ln_mod", x.device, x2.data_ptr(), _DTYPE_CODE[x.dtype], m, k, int(group), float(eps),
+              sc.data_ptr(), sh.data_ptr(), rows_per_vector, q.data_ptr(), s.data_ptr())
+    return q, s
+
+
 def int8_gemm_dequant(xq: torch.Tensor, xscale: torch.Tensor, wq: torch.Tensor, wscale: torch.Tensor,
                       bias: torch.Tensor | None, out_dtype: torch.dtype, out: torch.Tensor | None = None) -> torch.Tensor:
     """``((float(xq @ wq.T) * xscale[:, None]) * wscale[None, :]) + bias`` as ``out_dtype``.

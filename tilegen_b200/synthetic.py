@@ -9,6 +9,9 @@ generated on the CPU in fp32, then cast and moved):
   passed through the erf GELU.  Outlier channels: ``idx = randperm(K)[:round(p*K)]``
   and ``x[:, idx] *= s`` (p=1 %, s=30; FFN-down p=0.5 %, s=50).
 * weights ``W[N, K] ~ N(0, 0.02)``.
+* for the normalisation fused in front of a projection: a residual stream
+  (per-channel offsets, 0.5 % of channels x20) and adaLN modulation vectors
+  ``N(0, 0.1)`` (``residual_stream``, ``dit_modulation``).
 
 ``device="cuda"`` generates on the GPU instead (same distribution, different
 stream of numbers), which the benchmark uses for the large shapes.
@@ -71,3 +74,26 @@ def gaussian_weight(n: int, k: int, *, seed: int = 0, std: float = 0.02,
     dev = torch.device(device)
     w = torch.randn(n, k, generator=_gen(seed, dev), device=dev, dtype=torch.float32) * std
     return w.to(dtype)
+
+
+def residual_stream(m: int, k: int, *, seed: int = 0, dtype=torch.float16, device="cpu") -> torch.Tensor:
+    """A DiT block's residual stream ``h[m, k]`` (the input of its LayerNorm): per-channel
+    offsets ``N(0, 0.5)`` plus ``N(0, 1)`` noise, with 0.5 % of the channels x20 (the
+    large "massive activation" channels such streams carry)."""
+    dev = torch.device(device)
+    g = _gen(seed, dev)
+    offset = torch.randn(k, generator=g, device=dev) * 0.5
+    h = torch.randn(m, k, generator=g, device=dev) + offset
+    idx = torch.randperm(k, generator=g, device=dev)[: max(1, round(0.005 * k))]
+    h[:, idx] *= 20.0
+    return h.to(dtype)
+
+
+def dit_modulation(vectors: int, k: int, *, seed: int = 0, dtype=torch.float16, device="cpu"):
+    """``(scale, shift)``, each ``[vectors, k] ~ N(0, 0.1)``: the adaLN modulation a DiT
+    block applies after its LayerNorm, one vector per sample."""
+    dev = torch.device(device)
+    g = _gen(seed, dev)
+    scale = torch.randn(vectors, k, generator=g, device=dev) * 0.1
+    shift = torch.randn(vectors, k, generator=g, device=dev) * 0.1
+    return scale.to(dtype), shift.to(dtype)

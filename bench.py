@@ -592,6 +592,57 @@ def _input_act_table(dev, flush, stream, iters=20):
     return act_rows, rw_rows
 
 
+def _ln_mod_table(dev, flush, stream, iters=20):
+    """The DiT block's LayerNorm + adaLN modulation in front of qkv_proj at M = 4096
+    (two samples of 2048 tokens, one modulation vector each): fused into the
+    quantiser (``ops.quantize_ln_mod``) vs torch's ``F.layer_norm`` and the two
+    elementwise ops, then the quantiser; the quantisation alone and the whole
+    linear both ways, and the bf16 comparator (torch's ops, then cuBLAS)."""
+    import torch
+    import torch.nn.functional as F
+
+    from tilegen_b200 import ops
+    from tilegen_b200.synthetic import dit_modulation, gaussian_weight, residual_stream
+
+    m, k, n = M_PER_RANK, 5120, 15360
+
+    def timed(body):
+        def f(e):
+            e[0].record(stream)
+            body()
+            e[1].record(stream)
+
+        for _ in range(3):
+            f([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+        return round(statistics.median(r[0] for r in _time_steps(f, iters, flush, stream)) * 1e3, 2)
+
+    rows = []
+    w = gaussian_weight(n, k, seed=1, dtype=torch.bfloat16, device=dev)
+    wq, ws = ops.rotate_quant(w, GROUP)
+    for dt in (torch.float16, torch.bfloat16):
+        x = residual_stream(m, k, seed=0, dtype=dt, device=dev)
+        sc, sh = dit_modulation(2, k, seed=1, dtype=dt, device=dev)
+        x3, sc3, sh3 = x.view(2, m // 2, k), sc.view(2, 1, k), sh.view(2, 1, k)
+        wb = w.to(dt)
+
+        def norm_mod():  # the DiT block's own form: per-sample vectors broadcast over tokens
+            return (F.layer_norm(x3, (k,), eps=1e-6) * (1 + sc3) + sh3).view(m, k)
+
+        row = {"dtype": "fp16" if dt == torch.float16 else "bf16", "M": m, "K": k, "N": n, "vectors": 2}
+        row["quant_fused_us"] = timed(lambda: ops.quantize_ln_mod(x, GROUP, sc, sh))
+        row["quant_unfused_us"] = timed(lambda: ops.rotate_quant(norm_mod(), GROUP))
+        row["linear_fused_us"] = timed(
+            lambda: ops.int8_gemm_dequant(*ops.quantize_ln_mod(x, GROUP, sc, sh), wq, ws, None, dt))
+        row["linear_unfused_us"] = timed(
+            lambda: ops.int8_gemm_dequant(*ops.rotate_quant(norm_mod(), GROUP), wq, ws, None, dt))
+        row["bf16_norm_mod_cublas_us"] = timed(lambda: F.linear(norm_mod(), wb))
+        row["speedup_vs_bf16"] = round(row["bf16_norm_mod_cublas_us"] / row["linear_fused_us"], 3)
+        rows.append(row)
+        del x, wb
+    del w, wq, ws
+    return rows
+
+
 def _event_floor_us(dev, flush, stream, iters=30):
     """A one-element fill kernel timed like a single quantiser launch (between two
     events after an L2 flush): the fixed cost every such measurement carries."""
@@ -974,13 +1025,14 @@ def run_tilegen(args):
     int8_lib_tops = _int_mm_tops(dev)
     status = _lib.device_status(local)
 
-    shapes = cpu = sweep = act_table = small_m = None
+    shapes = cpu = sweep = act_table = small_m = ln_table = None
     event_floor = _event_floor_us(dev, flush, stream)
     if world == 1:
         shapes = _shape_table(dev, flush, stream)
         small_m = _small_m_table(dev, flush, peaks["hbm_gbs"])
         sweep = _quant_sweep(dev, flush, stream)
         act_table = _input_act_table(dev, flush, stream)
+        ln_table = _ln_mod_table(dev, flush, stream)
     # Last: seconds of sustained load that leave the GPU at its power cap.
     if world > 1:
         dist.barrier()
@@ -1069,6 +1121,8 @@ def run_tilegen(args):
                                                "speedup_vs_bf16", "weight_stream_frac_of_hbm"], "rows": small_m,
                                    "timing": "whole linears (rotate+quant + GEMM; bf16: F.linear) replayed 10 at a "
                                              "time from a CUDA graph, L2 flushed before each, flush time subtracted"}
+    if ln_table is not None:
+        line["norm_modulation_qkv"] = ln_table
     if act_table is not None:
         line["input_act_ffn_down"] = act_table[0]
         line["rowwise_quant"] = {"columns": ["K", "M", "dtype", "us", "GB/s", "frac_of_hbm"], "rows": act_table[1]}

@@ -270,25 +270,67 @@ static float round_to_dtype(float v, int dtype) {
 }
 
 /* Sum of one row's per-line partials part[0..lines) in the kernel's fixed
- * order: column c < 16 adds lines c, c + 16, c + 32, ... ascending, then the
- * column sums are added in ascending order. */
+ * order: column c < 16 adds lines c, c + 16, c + 32, ... ascending (columns
+ * past the lines are 0), then the 16 columns are added as a pairwise tree,
+ * ((c0 + c1) + (c2 + c3)) + ((c4 + c5) + (c6 + c7)) + ... . */
 static float ln_row_total(const float *part, int lines) {
-    const int cols = lines < 16 ? lines : 16;
-    float tot = 0.0f;
-    for (int c = 0; c < cols; ++c) {
+    float col[16];
+    for (int c = 0; c < 16; ++c) {
+        if (c >= lines) {
+            col[c] = 0.0f;
+            continue;
+        }
         float t = part[c];
         for (int l = c + 16; l < lines; l += 16) t += part[l];
-        tot = c == 0 ? t : tot + t;
+        col[c] = t;
     }
-    return tot;
+    float q[4];
+    for (int i = 0; i < 4; ++i) q[i] = (col[4 * i] + col[4 * i + 1]) + (col[4 * i + 2] + col[4 * i + 3]);
+    return (q[0] + q[1]) + (q[2] + q[3]);
+}
+
+/* 1 / sqrt(v) rounded to the nearest float (ties to even), as the kernel's
+ * correctly rounded reciprocal square root: a candidate from double
+ * precision, then the exact side of each neighbouring midpoint m from the sign
+ * of m*m*v - 1 (m*m is exact in double; one fma rounds the rest once, which
+ * keeps the sign). */
+static uint32_t f32_bits(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return u;
+}
+
+static float rsqrt_rn(float v) {
+    if (isnan(v) || v < 0.0f) return NAN;
+    if (v == 0.0f) return signbit(v) ? -INFINITY : INFINITY;
+    if (isinf(v)) return 0.0f;
+    float f = (float)(1.0 / sqrt((double)v));
+    for (int it = 0; it < 2; ++it) {
+        const float up = nextafterf(f, INFINITY);
+        const double mu = ((double)f + (double)up) * 0.5;
+        const double su = fma(mu * mu, (double)v, -1.0);  /* < 0: 1/sqrt(v) above the midpoint */
+        if (su < 0.0 || (su == 0.0 && (f32_bits(up) & 1u) == 0u)) {
+            f = up;
+            continue;
+        }
+        const float dn = nextafterf(f, 0.0f);
+        const double md = ((double)f + (double)dn) * 0.5;
+        const double sd = fma(md * md, (double)v, -1.0);  /* > 0: 1/sqrt(v) below the midpoint */
+        if (sd > 0.0 || (sd == 0.0 && (f32_bits(dn) & 1u) == 0u)) {
+            f = dn;
+            continue;
+        }
+        break;
+    }
+    return f;
 }
 
 /* y = dtype(dtype(dtype((x - mean) * rstd) * dtype(1 + scale[v])) + shift[v])
  * for row m and v = m / mod_rows, with, per row of K = 64 * lines values:
  *   line sums: pairs (2k, 2k+1) of the line's 64 values accumulated in two
- *     lanes, k ascending, then lane 0 + lane 1; mean = total(line sums) / K;
+ *     lanes, k ascending, then lane 0 + lane 1; mean = total(line sums) * RN(1/K);
  *   d = x - mean; line sums of squares the same way with fmaf(d, d, acc);
- *   var = total / K; rstd = 1 / sqrtf(var + eps);
+ *   var = total * RN(1/K); rstd = 1 / sqrt(var + eps) correctly rounded;
  * every operation in fp32 rounded once, then each named rounding to the dtype.
  * x, scale, shift, y hold raw fp16/bf16 patterns ([M][K], [.][K], [.][K], [M][K]).
  * Returns 0 on success, -1 on a bad argument. */
@@ -313,7 +355,8 @@ int oracle_ln_mod(const uint16_t *x, int dtype, int64_t M, int64_t K, float eps,
             }
             part[l] = a0 + a1;
         }
-        const float mean = ln_row_total(part, lines) / (float)K;
+        const float inv_k = 1.0f / (float)K;
+        const float mean = ln_row_total(part, lines) * inv_k;
         for (int l = 0; l < lines; ++l) {
             float q0 = 0.0f, q1 = 0.0f;
             for (int k = 0; k < 32; ++k) {
@@ -324,8 +367,8 @@ int oracle_ln_mod(const uint16_t *x, int dtype, int64_t M, int64_t K, float eps,
             }
             part[l] = q0 + q1;
         }
-        const float var = ln_row_total(part, lines) / (float)K;
-        const float rstd = 1.0f / sqrtf(var + eps);
+        const float var = ln_row_total(part, lines) * inv_k;
+        const float rstd = rsqrt_rn(var + eps);
         for (int l = 0; l < lines; ++l) {
             for (int j = 0; j < 64; ++j) d[j] = load_elem(x, dtype, m * K + l * 64 + j) - mean;
             for (int j = 0; j < 64; ++j) {

@@ -368,6 +368,7 @@ int quantize_launch(const void* x, int x_dtype, int64_t M, int64_t K, int group,
   p.mod_shift = ln ? ln->shift : nullptr;
   p.mod_rows = ln ? ln->rows : 1;
   p.ln_eps = ln ? ln->eps : 0.0f;
+  p.ln_inv_k = 1.0f / float(K);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf = x_dtype == TG_DT_BF16;

@@ -65,13 +65,14 @@ struct RotQuantParams {
   const void* mod_shift;
   int64_t mod_rows;
   float ln_eps;
+  float ln_inv_k;  // RN(1 / K): the mean and the variance are sums times it
 };
 
 // Words of shared memory the LayerNorm prologue needs beyond the ring, the
 // barriers and the row maxima: per-line partial sums of x and of (x - mean)^2
 // ([R][lines]) and their 16 column sums ([R][16]), for a CTA of `threads`
-// threads (lines <= threads / R).
-__host__ __device__ constexpr int ln_words(int threads, int R) { return 2 * threads + 2 * 16 * R; }
+// threads (lines <= threads / R), plus 4 words of slack to align them to 16 bytes.
+__host__ __device__ constexpr int ln_words(int threads, int R) { return 2 * threads + 2 * 16 * R + 4; }
 
 // Packed round-to-nearest add and multiply of two x-dtype pairs held as the
 // bits of 32-bit words.
@@ -95,26 +96,29 @@ __device__ __forceinline__ uint32_t hmul2_dt(uint32_t a, uint32_t b) {
 }
 
 // Sum of one row's per-line partials in a fixed order: column c < 16 of the
-// row adds lines c, c + 16, c + 32, ... (ascending), then every thread adds the
-// (up to) 16 column sums in ascending order.  Two CTA barriers; every thread of
-// the CTA must call it.  `part` [R][lines], `col` [R][16].
+// row adds lines c, c + 16, c + 32, ... (ascending) into col[c] (columns past
+// the row's lines stay 0: zeroed once at kernel start), then every thread adds
+// the 16 columns as a pairwise tree, ((c0 + c1) + (c2 + c3)) + ... .  Two CTA
+// barriers; every thread of the CTA must call it.  `part` [R][lines], `col`
+// [R][16] (16-byte aligned).
 __device__ __forceinline__ float row_total(float* part, float* col, float mine, bool active, int row_local,
                                            int chunk, int cpr) {
   if (active) part[row_local * cpr + chunk] = mine;
   __syncthreads();
-  const int cols = cpr < 16 ? cpr : 16;
-  if (active && chunk < cols) {
+  if (active && chunk < 16) {
     float t = part[row_local * cpr + chunk];
     for (int c = chunk + 16; c < cpr; c += 16) t = __fadd_rn(t, part[row_local * cpr + c]);
     col[row_local * 16 + chunk] = t;
   }
   __syncthreads();
-  float tot = 0.0f;
-  if (active) {
-    tot = col[row_local * 16];
-    for (int c = 1; c < cols; ++c) tot = __fadd_rn(tot, col[row_local * 16 + c]);
-  }
-  return tot;
+  const float4* c4 = reinterpret_cast<const float4*>(col + row_local * 16);
+  float4 v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = active ? c4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  float q[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = __fadd_rn(__fadd_rn(v[i].x, v[i].y), __fadd_rn(v[i].z, v[i].w));
+  return __fadd_rn(__fadd_rn(q[0], q[1]), __fadd_rn(q[2], q[3]));
 }
 
 // One radix-4 butterfly, each output evaluated exactly as
@@ -470,7 +474,8 @@ __global__ void __maxnreg__(REGS) rotquant_kernel(const __grid_constant__ CUtens
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(stages) * stage_bytes);
   unsigned* rowmax = reinterpret_cast<unsigned*>(full + stages);  // [3][R] maxima, then [3][R] NaN flags
-  float* const ln_area = reinterpret_cast<float*>(rowmax + 6 * R);  // kActLnMod: ln_words(blockDim.x, R)
+  // kActLnMod: ln_words(blockDim.x, R) words from here, 16-byte aligned.
+  float* const ln_area = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(rowmax + 6 * R) + 15) & ~uintptr_t(15));
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x;
@@ -484,6 +489,13 @@ __global__ void __maxnreg__(REGS) rotquant_kernel(const __grid_constant__ CUtens
     abort_flag = 0;
   }
   for (int i = tid; i < 6 * R; i += blockDim.x) rowmax[i] = 0u;
+  if constexpr (ACT == kActLnMod) {
+    // The column sums past a short row's lines are read as zeros, never written.
+    for (int i = tid; i < 16 * R; i += blockDim.x) {
+      ln_area[blockDim.x + i] = 0.0f;
+      ln_area[2 * blockDim.x + 16 * R + i] = 0.0f;
+    }
+  }
   __syncthreads();
   // Let the next kernel in the stream (the GEMM) be scheduled as SMs free up;
   // it waits for this grid's completion before reading the codes.  Then wait
@@ -557,11 +569,11 @@ __global__ void __maxnreg__(REGS) rotquant_kernel(const __grid_constant__ CUtens
     }
     if constexpr (ACT == kActLnMod) {
       // LayerNorm over the row (no affine), then the modulation, each result in
-      // x's dtype as the separate ops would store it: mean and variance in fp32
-      // summed in a fixed order (per line over its 64 values in pairs, then
-      // row_total), rstd = 1 / sqrt(var + eps), xn = dtype((x - mean) * rstd),
-      // y = dtype(dtype(xn * dtype(1 + scale)) + shift).  The last three are
-      // packed half-precision adds and multiplies: each gives the fp32 result
+      // x's dtype as the separate ops would store it: mean and variance in fp32,
+      // sums in a fixed order (per line over its 64 values in pairs, then
+      // row_total) times RN(1/K), rstd = RN(1 / sqrt(var + eps)),
+      // xn = dtype((x - mean) * rstd), y = dtype(dtype(xn * dtype(1 + scale)) + shift).
+      // The last three are packed half-precision adds and multiplies: each gives the fp32 result
       // rounded to the dtype, because 24 bits hold the exact product of two
       // 11-bit (or 8-bit) significands and rounding an fp32 sum or product
       // again to a format of at most 11 bits is innocuous (24 >= 2 * 11 + 2).
@@ -573,7 +585,7 @@ __global__ void __maxnreg__(REGS) rotquant_kernel(const __grid_constant__ CUtens
 #pragma unroll
       for (int k = 1; k < 32; ++k) a = add2(a, vp[k]);
       const float mean =
-          __fdiv_rn(row_total(part_s, col_s, __fadd_rn(a.x, a.y), active, row_local, chunk, cpr), float(K));
+          __fmul_rn(row_total(part_s, col_s, __fadd_rn(a.x, a.y), active, row_local, chunk, cpr), p.ln_inv_k);
       const float2 neg_mean = make_float2(-mean, -mean);
       float2 sq = make_float2(0.0f, 0.0f);
 #pragma unroll
@@ -582,8 +594,8 @@ __global__ void __maxnreg__(REGS) rotquant_kernel(const __grid_constant__ CUtens
         sq = fma2(vp[k], vp[k], sq);
       }
       const float var =
-          __fdiv_rn(row_total(part_q, col_q, __fadd_rn(sq.x, sq.y), active, row_local, chunk, cpr), float(K));
-      const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.ln_eps)));
+          __fmul_rn(row_total(part_q, col_q, __fadd_rn(sq.x, sq.y), active, row_local, chunk, cpr), p.ln_inv_k);
+      const float rstd = __frsqrt_rn(__fadd_rn(var, p.ln_eps));
       const float2 rstd2 = make_float2(rstd, rstd);
       // Modulation vector of this row (rows past M, which are never stored,
       // read the last row's).
@@ -593,17 +605,19 @@ __global__ void __maxnreg__(REGS) rotquant_kernel(const __grid_constant__ CUtens
       const uint4* scv = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.mod_scale) + voff);
       const uint4* shv = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.mod_shift) + voff);
       const uint32_t one2 = BF16 ? 0x3f803f80u : 0x3c003c00u;  // (1, 1) in the dtype
+      if (active) {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 sw = active ? __ldg(scv + c) : make_uint4(0u, 0u, 0u, 0u);
-        const uint4 hw = active ? __ldg(shv + c) : make_uint4(0u, 0u, 0u, 0u);
-        const uint32_t su[4] = {sw.x, sw.y, sw.z, sw.w};
-        const uint32_t hu[4] = {hw.x, hw.y, hw.z, hw.w};
+        for (int c = 0; c < 8; ++c) {
+          const uint4 sw = __ldg(scv + c);
+          const uint4 hw = __ldg(shv + c);
+          const uint32_t su[4] = {sw.x, sw.y, sw.z, sw.w};
+          const uint32_t hu[4] = {hw.x, hw.y, hw.z, hw.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t xn = pack2_dtype<BF16>(mul2(vp[4 * c + i], rstd2));
-          const uint32_t y = hadd2_dt<BF16>(hmul2_dt<BF16>(xn, hadd2_dt<BF16>(one2, su[i])), hu[i]);
-          vp[4 * c + i] = unpack2_dtype<BF16>(y);
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t xn = pack2_dtype<BF16>(mul2(vp[4 * c + i], rstd2));
+            const uint32_t y = hadd2_dt<BF16>(hmul2_dt<BF16>(xn, hadd2_dt<BF16>(one2, su[i])), hu[i]);
+            vp[4 * c + i] = unpack2_dtype<BF16>(y);
+          }
         }
       }
     }

@@ -106,8 +106,16 @@ __device__ __forceinline__ float row_total(float* part, float* col, float mine, 
   if (active) part[row_local * cpr + chunk] = mine;
   __syncthreads();
   if (active && chunk < 16) {
-    float t = part[row_local * cpr + chunk];
-    for (int c = chunk + 16; c < cpr; c += 16) t = __fadd_rn(t, part[row_local * cpr + c]);
+    // Loads four lines ahead of the (sequential) adds, so that their shared-
+    // memory latencies overlap while the other threads wait at the barrier.
+    const float* pr = part + row_local * cpr;
+    float t = pr[chunk];
+    int c = chunk + 16;
+    for (; c + 48 < cpr; c += 64) {
+      const float a = pr[c], b = pr[c + 16], d = pr[c + 32], e = pr[c + 48];
+      t = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(t, a), b), d), e);
+    }
+    for (; c < cpr; c += 16) t = __fadd_rn(t, pr[c]);
     col[row_local * 16 + chunk] = t;
   }
   __syncthreads();

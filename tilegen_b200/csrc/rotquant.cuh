@@ -482,8 +482,11 @@ __global__ void __maxnreg__(REGS) rotquant_kernel(const __grid_constant__ CUtens
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(stages) * stage_bytes);
   unsigned* rowmax = reinterpret_cast<unsigned*>(full + stages);  // [3][R] maxima, then [3][R] NaN flags
-  // kActLnMod: ln_words(blockDim.x, R) words from here, 16-byte aligned.
-  float* const ln_area = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(rowmax + 6 * R) + 15) & ~uintptr_t(15));
+  // kActLnMod: ln_words(blockDim.x, R) words after the row maxima, 16-byte
+  // aligned (an offset from the shared-memory base, so that the compiler keeps
+  // shared-memory loads and stores for them).
+  float* const ln_area = reinterpret_cast<float*>(
+      smem + ((size_t(stages) * stage_bytes + size_t(stages) * 8u + size_t(6 * R) * 4u + 15u) & ~size_t(15)));
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x;

@@ -154,3 +154,31 @@ def test_linear_with_fused_norm_matches_unfused(cuda):
     y_ref = ops.int8_gemm_dequant(rq, rs, wq, ws, None, torch.bfloat16)
     rel = float((y.float() - y_ref.float()).norm() / y_ref.float().norm())
     assert rel < 1e-3, rel
+
+
+def test_fused_linear_in_graph_matches_eager(cuda):
+    """The fused quantiser and the GEMM after it (its programmatic dependent),
+    captured in a CUDA graph and replayed: identical to the eager calls."""
+    from tilegen_b200.synthetic import gaussian_weight
+
+    m, k, n = 256, 5120, 640
+    x = residual_stream(m, k, seed=31, dtype=torch.float16, device=cuda)
+    scale, shift = dit_modulation(2, k, seed=32, dtype=torch.float16, device=cuda)
+    wq, ws = ops.rotate_quant(gaussian_weight(n, k, seed=33, dtype=torch.float16, device=cuda), 256)
+
+    def linear():
+        return ops.int8_gemm_dequant(*ops.quantize_ln_mod(x, 256, scale, shift), wq, ws, None, torch.float16)
+
+    eager = linear()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        linear()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        y = linear()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, eager)

@@ -138,9 +138,10 @@ def test_empty_and_rejects(cuda):
 
 
 def test_linear_with_fused_norm_matches_unfused(cuda):
-    """The qkv projection fed by the fused quantiser equals the projection of torch's
-    LayerNorm + modulation within the parity tolerance of its codes, and the GEMM
-    is the same: a bit-exact GEMM of the fused codes."""
+    """A projection fed by the fused quantiser is within 1e-3 (relative Frobenius) of
+    the same projection fed by torch's LayerNorm + modulation and the quantiser:
+    the few codes that differ by one move the output by far less than the int8
+    quantisation itself."""
     from tilegen_b200.synthetic import gaussian_weight
 
     m, k, n = 512, 5120, 1024

@@ -332,3 +332,19 @@ def test_host_linear_chunk_schedule_covers_rows():
             assert all(a[1] == b[0] and a[0] < a[1] for a, b in zip(ch, ch[1:] + [(m, m + 1)]))
             sizes = [b - a for a, b in ch]
             assert max(sizes) <= rows and sizes[0] == min(max(1, rows // 4), m)
+
+
+def test_custom_ops_trace_on_meta_tensors():
+    """The torch.library ops have shape functions, so they trace (torch.compile /
+    torch.export) without running a kernel: meta tensors in, meta tensors out."""
+    from tilegen_b200 import ops  # noqa: F401  (registers the ops)
+
+    x = torch.empty(2, 3, 512, dtype=torch.float16, device="meta")
+    vec = torch.empty(2, 1, 512, dtype=torch.float16, device="meta")
+    q, s = torch.ops.tilegen.quantize_ln_mod(x, 256, vec, vec, 1e-6)
+    assert q.shape == (6, 512) and q.dtype == torch.int8 and s.shape == (6,) and s.dtype == torch.float32
+    q, s = torch.ops.tilegen.quantize_act(x.view(6, 512), 256, "gelu_tanh")
+    assert q.shape == (6, 512) and s.shape == (6,)
+    y = torch.ops.tilegen.int8_gemm_dequant(q, s, torch.empty(8, 512, dtype=torch.int8, device="meta"),
+                                            torch.empty(8, device="meta"), None, torch.bfloat16)
+    assert y.shape == (6, 8) and y.dtype == torch.bfloat16

@@ -10,7 +10,8 @@ few-row GEMV on the CUDA cores; with up to ``SPLITK_MAX_M`` rows (see
 (device, stream); otherwise the tiled tcgen05 kernel.
 
 The same functions are registered as ``torch.ops.tilegen.rotate_quant``,
-``torch.ops.tilegen.quantize_act`` and ``torch.ops.tilegen.int8_gemm_dequant``
+``torch.ops.tilegen.quantize_act``, ``torch.ops.tilegen.quantize_ln_mod`` and
+``torch.ops.tilegen.int8_gemm_dequant``
 (with fake implementations, so they trace under ``torch.compile``/``torch.export``
 as opaque ops).
 """
@@ -332,6 +333,18 @@ def _quantize_act_op(x: torch.Tensor, group: int, act: str | None) -> tuple[torc
 @_quantize_act_op.register_fake
 def _(x, group, act):
     return x.new_empty(x.shape, dtype=torch.int8), x.new_empty((x.shape[0],), dtype=torch.float32)
+
+
+@torch.library.custom_op("tilegen::quantize_ln_mod", mutates_args=())
+def _quantize_ln_mod_op(x: torch.Tensor, group: int, scale: torch.Tensor, shift: torch.Tensor,
+                        eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    return quantize_ln_mod(x, group, scale, shift, eps)
+
+
+@_quantize_ln_mod_op.register_fake
+def _(x, group, scale, shift, eps):
+    m = x.numel() // x.shape[-1]
+    return x.new_empty((m, x.shape[-1]), dtype=torch.int8), x.new_empty((m,), dtype=torch.float32)
 
 
 @torch.library.custom_op("tilegen::int8_gemm_dequant", mutates_args=())

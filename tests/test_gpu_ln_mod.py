@@ -183,3 +183,11 @@ def test_fused_linear_in_graph_matches_eager(cuda):
         graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(y, eager)
+
+
+def test_custom_op_matches(cuda):
+    x = residual_stream(64, 3072, seed=41, dtype=torch.bfloat16, device=cuda)
+    sc, sh = dit_modulation(1, 3072, seed=42, dtype=torch.bfloat16, device=cuda)
+    a = torch.ops.tilegen.quantize_ln_mod(x, 256, sc, sh, 1e-6)
+    b = ops.quantize_ln_mod(x, 256, sc, sh, 1e-6)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])

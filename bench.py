@@ -217,8 +217,8 @@ def _setup_dist(args):
 
 
 def _reference_cpu():
-    """The reference's own CPU path of the linear (BASELINE plan: its eager
-    rotate+quant on the fp32-upcast activations, tilegen/kernels/int8_convrot.py:289-302,
+    """The reference's own CPU path of the linear (its eager rotate+quant on the
+    fp32-upcast activations, tilegen/kernels/int8_convrot.py:289-302,
     and its chunked GEMM + dequant on torch's CPU ``_int_mm``,
     tilegen/quant/int8_ops.py:22-70; the weight quantised offline by its
     quantize_convrot_weight, weight.py:14-39).

@@ -317,10 +317,10 @@ int quantize_launch(const void* x, int x_dtype, int64_t M, int64_t K, int group,
   // Rows per batch: the fewest that fill whole warps to within 5 %.
   int R = 1;
   for (int r = 1; r <= 8; ++r) {
-    const int act = r * cpr;
-    const int thr = (act + 31) / 32 * 32;
+    const int lines = r * cpr;
+    const int thr = (lines + 31) / 32 * 32;
     if (thr > 512) break;
-    if ((thr - act) * 20 <= act) {
+    if ((thr - lines) * 20 <= lines) {
       R = r;
       break;
     }
